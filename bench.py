@@ -1,0 +1,434 @@
+"""Benchmark of the krsi_b200 hot path on B200 (driver contract: one JSON line from rank 0).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload block|attn|attn_fwd|rmsnorm|geglu]
+  python bench.py --impl reference ...      # the reference's torch CPU path on the host cores
+  torchrun --nproc-per-node N bench.py --gpus N ...
+
+Workloads (all inputs synthetic, seeded, CPU-generated):
+  block     config 5: 28 pre-norm layers (RMSNorm -> qkv GEMM -> relpos attention -> out GEMM ->
+            +res -> RMSNorm -> wi GEMM -> GEGLU -> wo GEMM -> +res), x [32,1024,1152] bf16,
+            fwd+bwd with loss = mean(out.float()^2); batch-sharded over N ranks, NCCL all-reduce of
+            the weight gradients. Metric: tok/s (whole job). The default.
+  attn      config 4: relpos attention fwd+bwd, B=8 H=16 L=2048 D=72 bf16. TFLOP/s (12*B*H*L^2*D).
+  attn_fwd  config 3: relpos attention fwd, B=2 H=16 L=1024 D=72 bf16. TFLOP/s (4*B*H*L^2*D).
+  rmsnorm   config 1: RMSNorm fwd+bwd fp32 [2048,1152]. GB/s (algorithmic bytes).
+  geglu     config 2: GEGLU fwd+bwd bf16 [2048,9216]. GB/s (algorithmic bytes).
+For the op workloads a "step" is one fwd+bwd (or fwd) of the op; N>1 runs replicas (weak scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "kernel-rsi_b200"
+for _p in (str(ROOT), str(PKG), str(PKG / "library")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+L2_BYTES = 126 * 1024 * 1024
+
+
+# ---------------------------------------------------------------- environment helpers
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.is_file():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def ncu_traffic(kernel_key: str):
+    """DRAM bytes per launch of the dominant kernel from a committed ncu capture summary, or None."""
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    if not p.is_file():
+        return None
+    return json.loads(p.read_text()).get(kernel_key)
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.gpu)],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+        return False
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        loaded = [s for s in sm if mx and s > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def physical_gpu() -> str:
+    """nvidia-smi's id of this rank's GPU (CUDA_VISIBLE_DEVICES entry, else the local index)."""
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    vis = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    return vis[local].strip() if local < len(vis) else str(local)
+
+
+def cpu_info() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# ---------------------------------------------------------------- workloads
+# Each workload exposes: metric, unit, work_per_step (bytes or FLOP), setup(dev), step(),
+# e2e_step() (host buffers in, result read back), launches_per_step, dominant kernel timing,
+# and a CPU sample for the baseline.
+
+class OpWorkload:
+    higher_is_better = True
+    scaling = "weak"
+
+    def __init__(self, rank: int, world: int):
+        self.rank, self.world = rank, world
+        self.kernel_ms = []        # per-step device time of the dominant kernel (CUDA events)
+
+
+class RMSNormWorkload(OpWorkload):
+    name, metric, unit, dtype = "rmsnorm", "RMSNorm fwd+bwd throughput", "GB/s", "f32"
+    ROWS, N = 2048, 1152
+    # algorithmic bytes: fwd reads x, w, writes y, rstd; bwd reads g, x, w, rstd, writes dx, dw
+    FWD_B = ROWS * N * 4 * 2 + N * 4 + ROWS * 4
+    BWD_B = ROWS * N * 4 * 3 + N * 4 * 2 + ROWS * 4
+    work = FWD_B + BWD_B
+    launches_per_step = 3   # fwd, bwd rows, bwd dw reduction
+    kernel_key = "rmsnorm_fwd_bwd"
+
+    def config(self):
+        return {"workload": "rmsnorm fwd+bwd fp32 x[2,1024,1152] (config 1)", "rows": self.ROWS, "n": self.N,
+                "eps": 1e-6, "l2": "rotating input copies > L2"}
+
+    def setup_host(self):
+        from oracle import ops as O  # seeded input generator only
+
+        self.host = O.rmsnorm_inputs(self.ROWS, self.N, torch.float32, seed=0)
+
+    def setup(self, dev):
+        self.setup_host()
+        self.copies = max(2, math.ceil(3 * L2_BYTES / (3 * self.ROWS * self.N * 4)))
+        self.dev_inputs = [tuple(t.to(dev) for t in self.host) for _ in range(self.copies)]
+        self.i = 0
+        self.pinned = tuple(t.pin_memory() for t in self.host)
+
+    def step(self, timed=None):
+        x, w, g = self.dev_inputs[self.i % self.copies]
+        self.i += 1
+        if timed is not None:
+            timed[0].record()
+        y, rstd = torch.ops.krsi.rmsnorm_fwd(x, w, 1e-6)
+        dx, dw = torch.ops.krsi.rmsnorm_bwd(g, x, w, rstd)
+        if timed is not None:
+            timed[1].record()
+        return dx
+
+    def e2e_step(self, dev):
+        import rmsnorm
+
+        x, w, g = (t.to(dev, non_blocking=True) for t in self.pinned)
+        xr, wr = x.requires_grad_(True), w.requires_grad_(True)
+        y = rmsnorm.rmsnorm(xr, wr, 1e-6)
+        dx, dw = torch.autograd.grad(y, [xr, wr], g)
+        res = [y.detach().to("cpu"), dx.to("cpu"), dw.to("cpu")]
+        return res, sum(t.numel() * 4 for t in self.pinned), sum(t.numel() * 4 for t in res)
+
+    def cpu_sample(self):
+        from oracle import ops as O
+
+        x, w, g = self.host
+        xr, wr = x.clone().requires_grad_(True), w.clone().requires_grad_(True)
+        y = O.rmsnorm_reference(xr, wr, 1e-6)
+        torch.autograd.grad(y, [xr, wr], g)
+        return self.work, "one full fwd+bwd of config 1 (reference torch fp32 path)"
+
+
+class GegluWorkload(RMSNormWorkload):
+    name, metric, unit, dtype = "geglu", "GEGLU fwd+bwd throughput", "GB/s", "bf16"
+    ROWS, F = 2048, 4608
+    FWD_B = ROWS * 2 * F * 2 + ROWS * F * 2
+    BWD_B = ROWS * F * 2 + ROWS * 2 * F * 2 * 2
+    work = FWD_B + BWD_B
+    launches_per_step = 2
+    kernel_key = "geglu_fwd_bwd"
+
+    def config(self):
+        return {"workload": "geglu fwd+bwd bf16 u[2,1024,9216] (config 2)", "rows": self.ROWS, "F": self.F,
+                "l2": "rotating input copies > L2"}
+
+    def setup_host(self):
+        from oracle import ops as O
+
+        self.host = O.geglu_inputs(self.ROWS, self.F, torch.bfloat16, seed=0)
+
+    def setup(self, dev):
+        self.setup_host()
+        self.copies = max(2, math.ceil(3 * L2_BYTES / (3 * self.ROWS * self.F * 2)))
+        self.dev_inputs = [tuple(t.to(dev) for t in self.host) for _ in range(self.copies)]
+        self.i = 0
+        self.pinned = tuple(t.pin_memory() for t in self.host)
+
+    def step(self, timed=None):
+        u, g = self.dev_inputs[self.i % self.copies]
+        self.i += 1
+        if timed is not None:
+            timed[0].record()
+        out = torch.ops.krsi.geglu_fwd(u)
+        du = torch.ops.krsi.geglu_bwd(g, u)
+        if timed is not None:
+            timed[1].record()
+        return du
+
+    def e2e_step(self, dev):
+        import geglu
+
+        u, g = (t.to(dev, non_blocking=True) for t in self.pinned)
+        ur = u.requires_grad_(True)
+        out = geglu.geglu(ur)
+        (du,) = torch.autograd.grad(out, [ur], g)
+        res = [out.detach().to("cpu"), du.to("cpu")]
+        return res, sum(t.numel() * 2 for t in self.pinned), sum(t.numel() * 2 for t in res)
+
+    def cpu_sample(self):
+        from oracle import ops as O
+
+        u, g = (t.float() for t in self.host)
+        ur = u.clone().requires_grad_(True)
+        out = O.geglu_reference(ur)
+        torch.autograd.grad(out, [ur], g)
+        return self.work, "one full fwd+bwd of config 2 (reference torch path, fp32 on CPU)"
+
+
+WORKLOADS = {"rmsnorm": RMSNormWorkload, "geglu": GegluWorkload}
+
+
+def load_workloads():
+    try:
+        import bench_attn  # noqa: F401  (registers attn / attn_fwd / block when present)
+    except ImportError:
+        pass
+
+
+# ---------------------------------------------------------------- timing
+
+def time_steps(wl, steps, warmup, dev):
+    for _ in range(warmup):
+        wl.step()
+    torch.cuda.synchronize()
+    if dist.is_initialized():
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(physical_gpu()) as clk:
+        start.record()
+        for i in range(steps):
+            wl.step(timed=ev[i])
+        end.record()
+        torch.cuda.synchronize()
+    if dist.is_initialized():
+        dist.barrier()
+    total_ms = start.elapsed_time(end)
+    kernel_ms = [a.elapsed_time(b) for a, b in ev]
+    return total_ms, kernel_ms, clk.summary()
+
+
+def max_over_ranks(v: float) -> float:
+    if not dist.is_initialized():
+        return v
+    t = torch.tensor([v], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_baseline(wl, budget_s=15.0):
+    """The reference's torch CPU path on the host cores, bounded to about budget_s seconds."""
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    work, desc = wl.cpu_sample()             # warm-up call
+    t0 = time.perf_counter()
+    n, done = 0, 0.0
+    while True:
+        w, desc = wl.cpu_sample()
+        n += 1
+        done += w
+        if time.perf_counter() - t0 > budget_s or n >= 50:
+            break
+    dt = time.perf_counter() - t0
+    scale = 1e9 if wl.unit == "GB/s" else (1e12 if wl.unit == "TFLOP/s" else 1.0)
+    return {"value": done / dt / scale, "unit": wl.unit, "cores": threads, "kind": "port",
+            "sample": f"{n} x {desc}; {dt:.1f} s on {cpu_info()}"}
+
+
+# ---------------------------------------------------------------- arms
+
+def run_reference_arm(args, rank, world):
+    """--impl reference: the reference's CPU path (torch eager, as restated in oracle/) on the host
+    cores, rank 0 only; other ranks exit without work."""
+    if rank != 0:
+        return
+    load_workloads()
+    wl = WORKLOADS[args.workload](rank, world)
+    wl.setup_host()
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    for _ in range(args.warmup):
+        wl.cpu_sample()
+    t0 = time.perf_counter()
+    done, desc = 0.0, ""
+    for _ in range(args.steps):
+        w, desc = wl.cpu_sample()
+        done += w
+    dt = time.perf_counter() - t0
+    scale = 1e9 if wl.unit == "GB/s" else (1e12 if wl.unit == "TFLOP/s" else 1.0)
+    value = done / dt / scale
+    line = {"impl": "reference", "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / max(args.steps, 1),
+            "higher_is_better": wl.higher_is_better, "scaling": wl.scaling, "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded)", "config": wl.config(),
+            "cpu_baseline": {"value": value, "unit": wl.unit, "cores": threads, "kind": "port",
+                             "sample": f"{args.steps} x {desc} on {cpu_info()}"},
+            "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_krsi_arm(args, rank, world):
+    load_workloads()
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    import rmsnorm  # noqa: F401  (loads the native extension; fails loudly without it)
+
+    wl = WORKLOADS[args.workload](rank, world)
+    wl.setup(dev)
+    total_ms, kernel_ms, clocks = time_steps(wl, args.steps, args.warmup, dev)
+    ms = max_over_ranks(total_ms / args.steps)
+    scale = 1e9 if wl.unit == "GB/s" else (1e12 if wl.unit == "TFLOP/s" else 1.0)
+    per_step_work = wl.work * (world if wl.scaling == "weak" and wl.unit != "tok/s" else 1)
+    value = per_step_work / (ms / 1e3) / scale if wl.unit != "tok/s" else wl.tokens_per_step * world / (ms / 1e3)
+
+    # end to end through the public API, host buffers in and results out, every step
+    torch.cuda.synchronize()
+    if dist.is_initialized():
+        dist.barrier()
+    wl.e2e_step(dev)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e2e_steps = max(1, min(args.steps, 10))
+    h2d = d2h = 0
+    for _ in range(e2e_steps):
+        _, h2d, d2h = wl.e2e_step(dev)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / e2e_steps)
+    e2e_val = (per_step_work / (e2e_ms / 1e3) / scale if wl.unit != "tok/s"
+               else wl.tokens_per_step * world / (e2e_ms / 1e3))
+
+    # roofline of the dominant kernel (its own CUDA-event time inside the timed region)
+    pk = peaks()
+    kms = statistics.median(kernel_ms) if kernel_ms else None
+    roof = wl.roofline(kms, pk) if hasattr(wl, "roofline") else {
+        "bound": "hbm", "achieved": wl.work / (kms / 1e3) / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
+        "frac": wl.work / (kms / 1e3) / 1e9 / pk["hbm_gbs"], "traffic": ncu_traffic(wl.kernel_key),
+        "kernel": wl.kernel_key, "peak_source": pk["source"]}
+
+    if rank != 0:
+        return
+    line = {"metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": wl.higher_is_better,
+            "scaling": wl.scaling, "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded, CPU-generated)",
+            "config": wl.config(), "clocks": clocks,
+            "e2e": {"value": e2e_val, "unit": wl.unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": wl.launches_per_step * args.steps, "roofline": roof}
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(wl)
+    if hasattr(wl, "extra"):
+        line.update(wl.extra())
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="krsi", choices=["krsi", "reference"])
+    ap.add_argument("--workload", default=os.environ.get("KRSI_BENCH_WORKLOAD", "block"))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world > 1 and args.impl != "reference":
+        from datetime import timedelta
+
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+    try:
+        if args.impl == "reference":
+            run_reference_arm(args, rank, world)
+        else:
+            run_krsi_arm(args, rank, world)
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,120 @@
+/*
+ * krsi_b200.h - C ABI of the B200 (sm_100a) kernels behind kernel-rsi's library ops.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t, launches
+ * asynchronously on that stream, never synchronises, never allocates device memory and
+ * returns a krsi_status code (0 = success).  Callers own all buffers; kernels that need
+ * scratch memory take a caller-provided workspace whose size is reported by the matching
+ * *_workspace_size() query.  Calls run on the CUDA context current to the calling thread,
+ * and the stream must belong to that context.
+ *
+ * Each function names the reference interface it replaces (file:line inside the
+ * kernel-rsi project).  Tensor layouts are the reference's:
+ *   - rows are contiguous, row-major ("x2d" [rows, n], "u" [rows, 2F]);
+ *   - qkv is [B*S, 3*H*D] with row stride `qkv_row_stride` elements and column layout
+ *     [3][H][D]; out/out32 are [B*S, H*D] contiguous; lse and delta are [B*H, S];
+ *   - pd is the per-head, per-distance bias [H, 2S-1] fp32:
+ *     bias[h, i, j] = pd[h, j - i + S - 1].
+ */
+#ifndef KRSI_B200_H
+#define KRSI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes returned by every entry point. */
+typedef enum {
+  KRSI_OK = 0,
+  KRSI_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad size, stride or dtype combination   */
+  KRSI_ERR_UNSUPPORTED = 2,      /* valid for the reference, not implemented here         */
+  KRSI_ERR_MISALIGNED = 3,       /* pointer/stride alignment required by TMA or vector IO */
+  KRSI_ERR_WORKSPACE = 4,        /* workspace pointer null or smaller than required       */
+  KRSI_ERR_CUDA = 5,             /* a CUDA runtime/driver call failed (launch, attribute) */
+  KRSI_ERR_DEVICE_TIMEOUT = 6    /* a bounded device-side wait gave up (see status read)  */
+} krsi_status;
+
+/* Element types accepted by the entry points. */
+typedef enum { KRSI_F32 = 0, KRSI_BF16 = 1, KRSI_F16 = 2 } krsi_dtype;
+
+/* Human-readable text for a krsi_status value. */
+const char* krsi_error_string(int status);
+
+/* ABI version: major*10000 + minor*100 + patch. */
+int krsi_abi_version(void);
+
+/* Reads (and optionally clears) the device-side watchdog word of the current device:
+ * 0 when no bounded wait ever gave up, else a KRSI_ERR_DEVICE_TIMEOUT code with the
+ * waiting role in bits 8..15.  Synchronises the current device; not for hot paths. */
+int krsi_device_status(int* status_out, int clear);
+
+/* ---------------------------------------------------------------- RMSNorm
+ * y = w * (x * rstd).to(w.dtype), rstd = 1/sqrt(mean(x^2) + eps), per row.
+ * Replaces library/rmsnorm.py:81-86 (_fwd -> _rms_fwd, rmsnorm.py:49-58).
+ * x, y: [rows, n] of x_dtype; w: [n] of w_dtype; rstd: [rows] fp32. */
+int krsi_rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd,
+                     int64_t rows, int64_t n, float eps,
+                     int x_dtype, int w_dtype, cudaStream_t stream);
+
+/* Bytes of workspace krsi_rmsnorm_bwd needs (the per-block dw partial sums). */
+int krsi_rmsnorm_bwd_workspace_size(int64_t rows, int64_t n, size_t* bytes);
+
+/* dx = r*dn - x*r^3*mean(dn*x) with dn = (g*w) rounded to the promoted input type;
+ * dw = sum over rows of g * (x*r).to(w.dtype), reduced deterministically in two stages.
+ * Replaces library/rmsnorm.py:89-95 (_bwd -> _rms_bwd, rmsnorm.py:61-78, then dwp.sum(0)).
+ * g, x, dx: [rows, n] of x_dtype; w, dw: [n] of w_dtype; rstd: [rows] fp32. */
+int krsi_rmsnorm_bwd(const void* g, const void* x, const void* w, const float* rstd,
+                     void* dx, void* dw, void* workspace, size_t workspace_bytes,
+                     int64_t rows, int64_t n, int x_dtype, int w_dtype, cudaStream_t stream);
+
+/* ---------------------------------------------------------------- GEGLU
+ * out = gelu_tanh(u[:, :F]).to(dtype) * u[:, F:].
+ * Replaces library/geglu.py:209-215 (_fwd -> _geglu_fwd, geglu.py:181-189).
+ * u: [rows, 2F]; out: [rows, F]; both of `dtype`. */
+int krsi_geglu_fwd(const void* u, void* out, int64_t rows, int64_t F, int dtype,
+                   cudaStream_t stream);
+
+/* du = [d(gate) | d(value)] in one [rows, 2F] tensor.
+ * Replaces library/geglu.py:218-222 (_bwd -> _geglu_bwd, geglu.py:192-206).
+ * g: [rows, F]; u, du: [rows, 2F]; all of `dtype`. */
+int krsi_geglu_bwd(const void* g, const void* u, void* du, int64_t rows, int64_t F,
+                   int dtype, cudaStream_t stream);
+
+/* ---------------------------------------------------------------- relpos attention
+ * Flash attention with an additive Toeplitz bias, non-causal:
+ *   s2[i,j] = (q_i . k_j * scale + pd[h, j-i+S-1]) * log2(e),  p = softmax over j,
+ *   out = p @ v  (bf16 or f16, [B*S, H*D]),  out32 = same in fp32,
+ *   lse[b*H+h, i] = max_j s2 + log2(sum_j exp2(s2 - max))   (log2 domain).
+ * Replaces library/relpos_attention.py:132-140 (_forward -> _fwd, relpos_attention.py:26-59).
+ * D must be a multiple of 8 and <= 128; qkv_row_stride a multiple of 8; dtype BF16 or F16. */
+int krsi_relpos_attn_fwd(const void* qkv, int64_t qkv_row_stride, const float* pd,
+                         void* out, float* out32, float* lse,
+                         int64_t B, int64_t S, int64_t H, int64_t D, float scale,
+                         int dtype, cudaStream_t stream);
+
+/* Bytes of workspace krsi_relpos_attn_bwd needs (delta, fp32 dQ accumulator,
+ * per-tile dBias diagonal partials). */
+int krsi_relpos_attn_bwd_workspace_size(int64_t B, int64_t S, int64_t H, int64_t D,
+                                        size_t* bytes);
+
+/* Gradients of the forward above for upstream gradient dout [B*S, H*D] (contiguous):
+ *   dqkv [B*S, 3*H*D] (row stride dqkv_row_stride, same [3][H][D] column layout),
+ *   dpd  [H, 2S-1] fp32 = sum over batch of the diagonal sums of dS (unscaled).
+ * delta = rowsum(dout * out32) is computed from the fp32 copy of O.
+ * Replaces library/relpos_attention.py:143-157 (_backward_impl -> _bwd_dkdv :62-94,
+ * _bwd_dq :97-126 and the torch diagonal reduction :154-156). */
+int krsi_relpos_attn_bwd(const void* dout, const void* qkv, int64_t qkv_row_stride,
+                         const float* pd, const float* out32, const float* lse,
+                         void* dqkv, int64_t dqkv_row_stride, float* dpd,
+                         void* workspace, size_t workspace_bytes,
+                         int64_t B, int64_t S, int64_t H, int64_t D, float scale,
+                         int dtype, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KRSI_B200_H */

@@ -1,0 +1,380 @@
+// rmsnorm.cu - RMSNorm forward/backward for B200: 128-bit coalesced row kernels with the
+// rows held in registers, fp32 statistics, and a two-stage deterministic dweight reduction.
+//
+// Semantics follow library/rmsnorm.py of kernel-rsi:
+//   forward  (rmsnorm.py:49-58): r = 1/sqrt(sum(x^2)/n + eps); y = w * (x*r).to(w.dtype),
+//            stored in x's dtype; r saved per row in fp32.
+//   backward (rmsnorm.py:61-78, :95): n = (x*r).to(w.dtype); dw += g*n (fp32);
+//            dn = (g*w) rounded to the promoted type of g and w, then fp32;
+//            dx = r*dn - x*r^3*sum(dn*x)/n; dw = (sum of per-block partials).to(w.dtype).
+// Layout: a row is a contiguous run of n elements handled by TPR threads (one warp for
+// rows up to 512 packets, else a 256- or 1024-thread block).  Thread t owns NCH packets of
+// VEC elements at columns (c*TPR + t)*VEC, so each load/store instruction of a row group is
+// one fully coalesced 128-bit-per-thread transaction.  NCH is a compile-time constant, so
+// the row slice stays in registers.
+#include "common.cuh"
+
+namespace krsi {
+namespace {
+
+constexpr int kBwdMaxBlocks = 296;   // fixed cap (2 x 148 SMs): the dw partial count, and
+                                     // so the bits of dw, do not depend on the GPU model
+
+template <int TPR> struct RowCfg {
+  static constexpr int kThreads = TPR == 32 ? 256 : TPR;   // block size
+  static constexpr int kRowsPerBlock = kThreads / TPR;      // rows processed together
+};
+
+// Sum over the TPR threads that share a row (a warp, or the whole block).
+template <int TPR>
+__device__ __forceinline__ float row_sum(float v, float* red) {
+  if constexpr (TPR == 32) return warp_sum(v);
+  else return block_sum<TPR>(v, red);
+}
+
+// Loads VEC consecutive elements of type T starting at p (16-byte aligned when VEC > 1).
+template <int DT, int VEC>
+__device__ __forceinline__ void load_vec(const typename Elem<DT>::T* p, float* out, bool stream) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  if constexpr (VEC == 1) {
+    out[0] = E::load(*p);
+  } else {
+    constexpr int PK = Vec16<T>::N;   // elements per 16-byte packet of this type
+#pragma unroll
+    for (int e = 0; e < VEC; e += PK) {
+      const auto v = stream ? ldg16_stream(p + e) : ldg16(p + e);
+#pragma unroll
+      for (int k = 0; k < PK; ++k) out[e + k] = E::load(v.v[k]);
+    }
+  }
+}
+
+template <int DT, int VEC>
+__device__ __forceinline__ void store_vec(typename Elem<DT>::T* p, const float* in) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  if constexpr (VEC == 1) {
+    *p = E::store(in[0]);
+  } else {
+    Vec16<T> o;
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) o.v[k] = E::store(in[k]);
+    stg16(p, o);
+  }
+}
+
+template <int XT, int WT, int TPR, int VEC, int NCH>
+__global__ void __launch_bounds__(RowCfg<TPR>::kThreads)
+rms_fwd_kernel(const typename Elem<XT>::T* __restrict__ x, const typename Elem<WT>::T* __restrict__ w,
+               typename Elem<XT>::T* __restrict__ y, float* __restrict__ rstd, int64_t rows, int n, float eps) {
+  using WE = Elem<WT>;
+  __shared__ float red[32];
+  const int t = threadIdx.x % TPR;
+  const int64_t row = (int64_t)blockIdx.x * RowCfg<TPR>::kRowsPerBlock + threadIdx.x / TPR;
+  const bool live = row < rows;   // a block-per-row group is always live
+  const auto* xr = x + row * n;
+  float xv[NCH][VEC];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int col = (c * TPR + t) * VEC;
+    if (live && col < n) {
+      load_vec<XT, VEC>(xr + col, xv[c], true);
+    } else {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) xv[c][e] = 0.f;
+    }
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) ss = fmaf(xv[c][e], xv[c][e], ss);
+  }
+  ss = row_sum<TPR>(ss, red);
+  const float r = 1.0f / sqrtf(ss / (float)n + eps);
+  if (!live) return;
+  if (t == 0) rstd[row] = r;
+  auto* yr = y + row * n;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int col = (c * TPR + t) * VEC;
+    if (col < n) {
+      float wv[VEC], o[VEC];
+      load_vec<WT, VEC>(w + col, wv, false);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) o[e] = WE::round(wv[e] * WE::round(xv[c][e] * r));
+      store_vec<XT, VEC>(yr + col, o);
+    }
+  }
+}
+
+template <int XT, int WT, int TPR, int VEC, int NCH>
+__global__ void __launch_bounds__(RowCfg<TPR>::kThreads)
+rms_bwd_kernel(const typename Elem<XT>::T* __restrict__ g, const typename Elem<XT>::T* __restrict__ x,
+               const typename Elem<WT>::T* __restrict__ w, const float* __restrict__ rstd,
+               typename Elem<XT>::T* __restrict__ dx, float* __restrict__ dw_part, int64_t rows, int n) {
+  using WE = Elem<WT>;
+  using DE = Elem<Promote<XT, WT>::value>;   // dtype of the g*w product
+  constexpr int RPB = RowCfg<TPR>::kRowsPerBlock;
+  extern __shared__ float smem_dw[];          // [RPB][n] when RPB > 1
+  __shared__ float red[32];
+  const int t = threadIdx.x % TPR;
+  const int sub = threadIdx.x / TPR;
+
+  float dwv[NCH][VEC];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) dwv[c][e] = 0.f;
+
+  for (int64_t row0 = (int64_t)blockIdx.x * RPB; row0 < rows; row0 += (int64_t)gridDim.x * RPB) {
+    const int64_t row = row0 + sub;
+    const bool live = row < rows;
+    const auto* xr = x + row * n;
+    const auto* gr = g + row * n;
+    float xv[NCH][VEC], dn[NCH][VEC];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int col = (c * TPR + t) * VEC;
+      if (live && col < n) {
+        load_vec<XT, VEC>(xr + col, xv[c], true);
+        load_vec<XT, VEC>(gr + col, dn[c], true);   // dn holds g until converted below
+      } else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) { xv[c][e] = 0.f; dn[c][e] = 0.f; }
+      }
+    }
+    const float r = live ? rstd[row] : 0.f;
+    float dot = 0.f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int col = (c * TPR + t) * VEC;
+      float wv[VEC];
+      if (col < n) load_vec<WT, VEC>(w + col, wv, false);
+      else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) wv[e] = 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        const float gg = dn[c][e];
+        dwv[c][e] = fmaf(gg, WE::round(xv[c][e] * r), dwv[c][e]);
+        dn[c][e] = DE::round(gg * wv[e]);
+        dot = fmaf(dn[c][e], xv[c][e], dot);
+      }
+    }
+    dot = row_sum<TPR>(dot, red);
+    const float k = r * r * r * (dot / (float)n);
+    if (live) {
+      auto* dxr = dx + row * n;
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        const int col = (c * TPR + t) * VEC;
+        if (col < n) {
+          float o[VEC];
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) o[e] = r * dn[c][e] - xv[c][e] * k;
+          store_vec<XT, VEC>(dxr + col, o);
+        }
+      }
+    }
+  }
+
+  // Per-block dw partial; the RPB row groups of a block are combined in a fixed order.
+  float* out = dw_part + (int64_t)blockIdx.x * n;
+  float* dst = RPB == 1 ? out : smem_dw + sub * n;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      const int col = (c * TPR + t) * VEC + e;
+      if (col < n) dst[col] = dwv[c][e];
+    }
+  if constexpr (RPB > 1) {
+    __syncthreads();
+    for (int col = threadIdx.x; col < n; col += blockDim.x) {
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < RPB; ++i) s += smem_dw[i * n + col];
+      out[col] = s;
+    }
+  }
+}
+
+// Stage 2 of dw: dw[col] = sum over the partial rows in a fixed order, rounded to w's dtype.
+// A block covers 32 columns with 8 warps; warp i sums partial rows i, i+8, ...; the eight
+// warp sums are then added in index order.
+template <int WT>
+__global__ void __launch_bounds__(256)
+rms_dw_reduce_kernel(const float* __restrict__ part, typename Elem<WT>::T* __restrict__ dw, int nparts, int n) {
+  __shared__ float acc[8][33];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int col = blockIdx.x * 32 + lane;
+  float s = 0.f;
+  if (col < n)
+    for (int p = wid; p < nparts; p += 8) s += part[(int64_t)p * n + col];
+  acc[wid][lane] = s;
+  __syncthreads();
+  if (wid == 0 && col < n) {
+    float tsum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tsum += acc[i][lane];
+    dw[col] = Elem<WT>::store(tsum);
+  }
+}
+
+// ---------------------------------------------------------------- host-side planning
+struct Plan {
+  int tpr, vec, nch;
+};
+
+inline int elem_size(int dt) { return dt == KRSI_F32 ? 4 : 2; }
+
+// Warp-per-row chunk counts that are compiled; a needed count is rounded up to the next.
+constexpr int kWarpNch[] = {1, 2, 3, 4, 6, 8, 9, 12, 16};
+constexpr int kBlockNch[] = {1, 2, 4, 8, 16};
+
+inline bool plan_rows(int64_t n, int x_dtype, bool vec_ok, Plan* p) {
+  p->vec = vec_ok ? 16 / elem_size(x_dtype) : 1;
+  const int64_t need32 = (n + 32 * p->vec - 1) / (32 * p->vec);
+  for (int c : kWarpNch)
+    if (c >= need32) { p->tpr = 32; p->nch = c; return true; }
+  for (int tp : {256, 1024}) {
+    const int64_t need = (n + (int64_t)tp * p->vec - 1) / ((int64_t)tp * p->vec);
+    for (int c : kBlockNch)
+      if (c >= need) { p->tpr = tp; p->nch = c; return true; }
+  }
+  return false;
+}
+
+inline int64_t bwd_blocks(int64_t rows, const Plan& p) {
+  const int rpb = p.tpr == 32 ? RowCfg<32>::kRowsPerBlock : 1;
+  const int64_t need = (rows + rpb - 1) / rpb;
+  return need < kBwdMaxBlocks ? need : kBwdMaxBlocks;
+}
+
+struct FwdArgs {
+  const void* x; const void* w; void* y; float* rstd; int64_t rows; int n; float eps; cudaStream_t s;
+};
+struct BwdArgs {
+  const void* g; const void* x; const void* w; const float* rstd; void* dx; void* dw; float* part;
+  int64_t nblocks; int64_t rows; int n; cudaStream_t s;
+};
+
+template <int XT, int WT, int TPR, int VEC, int NCH>
+int run_fwd(const FwdArgs& a) {
+  using Cfg = RowCfg<TPR>;
+  const int64_t grid = (a.rows + Cfg::kRowsPerBlock - 1) / Cfg::kRowsPerBlock;
+  if (grid > 0x7fffffff) return KRSI_ERR_UNSUPPORTED;
+  rms_fwd_kernel<XT, WT, TPR, VEC, NCH><<<(unsigned)grid, Cfg::kThreads, 0, a.s>>>(
+      (const typename Elem<XT>::T*)a.x, (const typename Elem<WT>::T*)a.w, (typename Elem<XT>::T*)a.y, a.rstd,
+      a.rows, a.n, a.eps);
+  KRSI_LAUNCH_CHECK();
+  return KRSI_OK;
+}
+
+template <int XT, int WT, int TPR, int VEC, int NCH>
+int run_bwd(const BwdArgs& a) {
+  using Cfg = RowCfg<TPR>;
+  const size_t smem = Cfg::kRowsPerBlock > 1 ? (size_t)Cfg::kRowsPerBlock * a.n * sizeof(float) : 0;
+  auto kern = rms_bwd_kernel<XT, WT, TPR, VEC, NCH>;
+  if (smem > 48 * 1024)
+    KRSI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  kern<<<(unsigned)a.nblocks, Cfg::kThreads, smem, a.s>>>(
+      (const typename Elem<XT>::T*)a.g, (const typename Elem<XT>::T*)a.x, (const typename Elem<WT>::T*)a.w,
+      a.rstd, (typename Elem<XT>::T*)a.dx, a.part, a.rows, a.n);
+  KRSI_LAUNCH_CHECK();
+  rms_dw_reduce_kernel<WT><<<(unsigned)((a.n + 31) / 32), 256, 0, a.s>>>(a.part, (typename Elem<WT>::T*)a.dw,
+                                                                         (int)a.nblocks, a.n);
+  KRSI_LAUNCH_CHECK();
+  return KRSI_OK;
+}
+
+// Runtime (tpr, nch) -> template instance, for one (XT, WT, VEC).
+template <int XT, int WT, int VEC, bool FWD, class Args>
+int dispatch_shape(const Plan& p, const Args& a) {
+#define KRSI_RUN(TPR, NCH) \
+  if constexpr (FWD) return run_fwd<XT, WT, TPR, VEC, NCH>(a); else return run_bwd<XT, WT, TPR, VEC, NCH>(a)
+  if (p.tpr == 32) {
+    switch (p.nch) {
+      case 1: KRSI_RUN(32, 1); case 2: KRSI_RUN(32, 2); case 3: KRSI_RUN(32, 3);
+      case 4: KRSI_RUN(32, 4); case 6: KRSI_RUN(32, 6); case 8: KRSI_RUN(32, 8);
+      case 9: KRSI_RUN(32, 9); case 12: KRSI_RUN(32, 12); case 16: KRSI_RUN(32, 16);
+    }
+  } else if (p.tpr == 256) {
+    switch (p.nch) {
+      case 1: KRSI_RUN(256, 1); case 2: KRSI_RUN(256, 2); case 4: KRSI_RUN(256, 4);
+      case 8: KRSI_RUN(256, 8); case 16: KRSI_RUN(256, 16);
+    }
+  } else if (p.tpr == 1024) {
+    switch (p.nch) {
+      case 1: KRSI_RUN(1024, 1); case 2: KRSI_RUN(1024, 2); case 4: KRSI_RUN(1024, 4);
+      case 8: KRSI_RUN(1024, 8); case 16: KRSI_RUN(1024, 16);
+    }
+  }
+#undef KRSI_RUN
+  return KRSI_ERR_UNSUPPORTED;
+}
+
+template <bool FWD, class Args>
+int dispatch(int x_dtype, int w_dtype, const Plan& p, const Args& a) {
+#define KRSI_DT(XT, WT, VW)                                                     \
+  if (x_dtype == XT && w_dtype == WT)                                           \
+    return p.vec == 1 ? dispatch_shape<XT, WT, 1, FWD>(p, a) : dispatch_shape<XT, WT, VW, FWD>(p, a)
+  KRSI_DT(KRSI_F32, KRSI_F32, 4);
+  KRSI_DT(KRSI_BF16, KRSI_BF16, 8);
+  KRSI_DT(KRSI_F16, KRSI_F16, 8);
+  KRSI_DT(KRSI_BF16, KRSI_F32, 8);
+  KRSI_DT(KRSI_F16, KRSI_F32, 8);
+#undef KRSI_DT
+  return KRSI_ERR_UNSUPPORTED;
+}
+
+inline bool dtype_ok(int d) { return d == KRSI_F32 || d == KRSI_BF16 || d == KRSI_F16; }
+
+}  // namespace
+}  // namespace krsi
+
+using namespace krsi;
+
+extern "C" int krsi_rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int64_t rows, int64_t n,
+                                float eps, int x_dtype, int w_dtype, cudaStream_t stream) {
+  KRSI_CHECK_ARG(rows >= 0 && n >= 0 && dtype_ok(x_dtype) && dtype_ok(w_dtype));
+  if (rows == 0) return KRSI_OK;
+  KRSI_CHECK_ARG(n > 0 && x && w && y && rstd);
+  if (n > 0x7fffffff) return KRSI_ERR_UNSUPPORTED;
+  const int vw = 16 / elem_size(x_dtype);
+  const bool vec_ok = (n % vw == 0) && aligned16(x) && aligned16(y) && aligned16(w);
+  Plan p;
+  if (!plan_rows(n, x_dtype, vec_ok, &p)) return KRSI_ERR_UNSUPPORTED;
+  return dispatch<true>(x_dtype, w_dtype, p, FwdArgs{x, w, y, rstd, rows, (int)n, eps, stream});
+}
+
+extern "C" int krsi_rmsnorm_bwd_workspace_size(int64_t rows, int64_t n, size_t* bytes) {
+  KRSI_CHECK_ARG(rows >= 0 && n >= 0 && bytes);
+  if (n > 0x7fffffff) return KRSI_ERR_UNSUPPORTED;
+  // Upper bound over every plan (the block-per-row plans use one row per block).
+  const int64_t nb = rows < kBwdMaxBlocks ? rows : kBwdMaxBlocks;
+  *bytes = (size_t)nb * (size_t)n * sizeof(float);
+  return KRSI_OK;
+}
+
+extern "C" int krsi_rmsnorm_bwd(const void* g, const void* x, const void* w, const float* rstd, void* dx, void* dw,
+                                void* workspace, size_t workspace_bytes, int64_t rows, int64_t n, int x_dtype,
+                                int w_dtype, cudaStream_t stream) {
+  KRSI_CHECK_ARG(rows >= 0 && n >= 0 && dtype_ok(x_dtype) && dtype_ok(w_dtype));
+  if (n == 0) return KRSI_OK;
+  KRSI_CHECK_ARG(w && dw);
+  if (n > 0x7fffffff) return KRSI_ERR_UNSUPPORTED;
+  if (rows == 0) {  // dw of an empty batch is zero
+    KRSI_CUDA_TRY(cudaMemsetAsync(dw, 0, (size_t)n * elem_size(w_dtype), stream));
+    return KRSI_OK;
+  }
+  KRSI_CHECK_ARG(g && x && rstd && dx);
+  const int vw = 16 / elem_size(x_dtype);
+  const bool vec_ok = (n % vw == 0) && aligned16(x) && aligned16(g) && aligned16(dx) && aligned16(w);
+  Plan p;
+  if (!plan_rows(n, x_dtype, vec_ok, &p)) return KRSI_ERR_UNSUPPORTED;
+  const int64_t nblocks = bwd_blocks(rows, p);
+  if (!workspace || workspace_bytes < (size_t)nblocks * (size_t)n * sizeof(float)) return KRSI_ERR_WORKSPACE;
+  return dispatch<false>(x_dtype, w_dtype, p,
+                         BwdArgs{g, x, w, rstd, dx, dw, static_cast<float*>(workspace), nblocks, rows, (int)n, stream});
+}

@@ -1,0 +1,63 @@
+"""The C ABI library: it loads without a GPU, exports every function include/krsi_b200.h declares,
+and rejects bad arguments with the documented status codes before touching the device."""
+import ctypes
+import re
+
+import pytest
+
+from conftest import PKG, ROOT
+
+HEADER = ROOT / "include" / "krsi_b200.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(krsi_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return ctypes.CDLL(str(PKG / "lib" / "libkrsi_b200.so"))
+
+
+def test_header_declares_the_hot_path():
+    names = declared_functions()
+    for op in ("rmsnorm_fwd", "rmsnorm_bwd", "geglu_fwd", "geglu_bwd", "relpos_attn_fwd", "relpos_attn_bwd"):
+        assert f"krsi_{op}" in names
+
+
+def test_every_declared_symbol_is_exported(lib):
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_error_strings_and_version(lib):
+    lib.krsi_error_string.restype = ctypes.c_char_p
+    for code in range(0, 7):
+        assert lib.krsi_error_string(code)
+    assert b"unknown" in lib.krsi_error_string(99)
+    assert lib.krsi_abi_version() >= 10000
+
+
+def test_argument_checks_return_codes(lib):
+    i64, vp = ctypes.c_int64, ctypes.c_void_p
+    # null pointers with real sizes -> INVALID_ARGUMENT (1), before any CUDA call
+    rc = lib.krsi_rmsnorm_fwd(vp(0), vp(0), vp(0), vp(0), i64(4), i64(8), ctypes.c_float(1e-6), 0, 0, vp(0))
+    assert rc == 1
+    rc = lib.krsi_geglu_fwd(vp(0), vp(0), i64(4), i64(8), 1, vp(0))
+    assert rc == 1
+    # bad dtype code
+    rc = lib.krsi_geglu_bwd(vp(1), vp(1), vp(1), i64(4), i64(8), 7, vp(0))
+    assert rc == 1
+    # empty inputs are a successful no-op
+    assert lib.krsi_rmsnorm_fwd(vp(0), vp(0), vp(0), vp(0), i64(0), i64(8), ctypes.c_float(1e-6), 0, 0, vp(0)) == 0
+    assert lib.krsi_geglu_fwd(vp(0), vp(0), i64(0), i64(8), 1, vp(0)) == 0
+
+
+def test_workspace_queries(lib):
+    sz = ctypes.c_size_t(0)
+    assert lib.krsi_rmsnorm_bwd_workspace_size(ctypes.c_int64(2048), ctypes.c_int64(1152), ctypes.byref(sz)) == 0
+    assert sz.value == 296 * 1152 * 4
+    assert lib.krsi_rmsnorm_bwd_workspace_size(ctypes.c_int64(3), ctypes.c_int64(10), ctypes.byref(sz)) == 0
+    assert sz.value == 3 * 10 * 4

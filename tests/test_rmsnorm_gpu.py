@@ -1,0 +1,124 @@
+"""RMSNorm CUDA kernels vs the oracle and the reference's criterion (B200)."""
+import ctypes
+
+import pytest
+import torch
+
+from gpu_util import DT, capi, ptr, reference_compare, stream
+from oracle import ops as O
+from oracle.compare import max_abs_err, norm_max_err
+
+pytestmark = pytest.mark.gpu
+dev = "cuda"
+
+
+def krsi():
+    import rmsnorm
+    return rmsnorm
+
+
+def test_baseline_config_fp32_max_abs_1e5():
+    """Config 1: x [2,1024,1152] fp32 ~ N(0,1), w = 1 + N(0,0.02), eps 1e-6, g ~ N(0,1):
+    output and both gradients within max-abs 1e-5 of the fp32 reference path."""
+    x, w, g = O.rmsnorm_inputs(2048, 1152, torch.float32, seed=0)
+    xd, wd, gd = x.to(dev), w.to(dev), g.to(dev)
+    y, rstd = torch.ops.krsi.rmsnorm_fwd(xd, wd, 1e-6)
+    dx, dw = torch.ops.krsi.rmsnorm_bwd(gd, xd, wd, rstd)
+    y_o, r_o = O.rmsnorm_fwd(x, w, 1e-6)
+    dx_o, dw_o = O.rmsnorm_bwd(g, x, w, r_o)
+    assert max_abs_err(y.cpu(), y_o) <= 1e-5
+    assert max_abs_err(rstd.cpu(), r_o) <= 1e-5
+    assert max_abs_err(dx.cpu(), dx_o) <= 1e-5
+    # dw sums 2048 rows: compare against the fp64 oracle relative to its magnitude
+    assert norm_max_err(dw.cpu(), dw_o) <= 1e-5
+    # through the autograd Function, against the reference's eager expression in fp32
+    xr = xd.clone().requires_grad_(True)
+    wr = wd.clone().requires_grad_(True)
+    out = krsi().rmsnorm(xr, wr, 1e-6)
+    gx, gw = torch.autograd.grad(out, [xr, wr], gd)
+    ref = O.rmsnorm_reference(x.double(), w.double(), 1e-6).float()
+    assert max_abs_err(out.cpu(), ref) <= 1e-5
+    assert max_abs_err(gx.cpu(), dx_o) <= 1e-5
+
+
+@pytest.mark.parametrize("rows,n,xdt,wdt", [
+    (4096, 1024, torch.bfloat16, torch.bfloat16),   # the reference's selftest shape
+    (300, 1152, torch.bfloat16, torch.bfloat16),
+    (1, 1152, torch.float32, torch.float32),
+    (33, 17, torch.float32, torch.float32),          # n not a multiple of the vector width
+    (7, 4096, torch.float16, torch.float16),
+    (5, 16384, torch.float32, torch.float32),        # block-per-row plan
+    (64, 1152, torch.bfloat16, torch.float32),       # mixed: bf16 activations, fp32 weight
+])
+def test_kernel_semantics_vs_oracle(rows, n, xdt, wdt):
+    x, w, g = O.rmsnorm_inputs(rows, n, torch.float32, seed=rows + n)
+    x, w, g = x.to(xdt), w.to(wdt), g.to(xdt)
+    y, rstd = torch.ops.krsi.rmsnorm_fwd(x.to(dev), w.to(dev), 1e-6)
+    dx, dw = torch.ops.krsi.rmsnorm_bwd(g.to(dev), x.to(dev), w.to(dev), rstd)
+    y_o, r_o = O.rmsnorm_fwd(x, w, 1e-6)
+    dx_o, dw_o = O.rmsnorm_bwd(g, x, w, r_o)
+    tol = 1e-5 if xdt == torch.float32 else 1e-2
+    assert norm_max_err(y.cpu(), y_o) <= tol
+    assert norm_max_err(rstd.cpu(), r_o) <= 1e-6
+    assert norm_max_err(dx.cpu(), dx_o) <= tol
+    assert norm_max_err(dw.cpu(), dw_o) <= (1e-5 if wdt == torch.float32 else 1e-2)
+
+
+def test_reference_selftest_criterion_bf16():
+    """The reference's selftest: [4096,1024] bf16, w = 1 + 0.1 N(0,1); compare() slack 2."""
+    x, w, _ = O.rmsnorm_inputs(4096, 1024, torch.float32, seed=3)
+    w = 1 + 0.1 * (w - 1) / 0.02
+    cot = O.gen((4096, 1024), 9, std=1e-2).to(dev)
+    res, _, _ = reference_compare(lambda a, b: krsi().rmsnorm(a, b, 1e-6), lambda a, b: O.rmsnorm_reference(a, b, 1e-6),
+                                  [x.to(dev, torch.bfloat16), w.to(dev, torch.bfloat16)], cot)
+    assert res["pass"], res
+
+
+def test_deterministic_and_graph_capturable():
+    x, w, g = (t.to(dev) for t in O.rmsnorm_inputs(2048, 1152, torch.float32, seed=1))
+    y1, r1 = torch.ops.krsi.rmsnorm_fwd(x, w, 1e-6)
+    dx1, dw1 = torch.ops.krsi.rmsnorm_bwd(g, x, w, r1)
+    dx2, dw2 = torch.ops.krsi.rmsnorm_bwd(g, x, w, r1)
+    assert torch.equal(dx1, dx2) and torch.equal(dw1, dw2)
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        torch.ops.krsi.rmsnorm_bwd(g, x, w, r1)
+    torch.cuda.current_stream().wait_stream(s)
+    with torch.cuda.graph(graph):
+        dx3, dw3 = torch.ops.krsi.rmsnorm_bwd(g, x, w, r1)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(dx3, dx1) and torch.equal(dw3, dw1)
+
+
+def test_c_abi_direct_call_matches_op():
+    """Call krsi_rmsnorm_fwd through ctypes with device pointers (no torch binding in between)."""
+    lib = capi()
+    x, w, _ = (t.to(dev) for t in O.rmsnorm_inputs(64, 1152, torch.float32, seed=2))
+    y = torch.empty_like(x)
+    rstd = torch.empty(64, device=dev)
+    rc = lib.krsi_rmsnorm_fwd(ptr(x), ptr(w), ptr(y), ptr(rstd), ctypes.c_int64(64), ctypes.c_int64(1152),
+                              ctypes.c_float(1e-6), DT[torch.float32], DT[torch.float32], stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    y2, r2 = torch.ops.krsi.rmsnorm_fwd(x, w, 1e-6)
+    assert torch.equal(y, y2) and torch.equal(rstd, r2)
+    # too small a workspace is refused
+    dx = torch.empty_like(x)
+    dw = torch.empty_like(w)
+    rc = lib.krsi_rmsnorm_bwd(ptr(x), ptr(x), ptr(w), ptr(rstd), ptr(dx), ptr(dw), ptr(x), ctypes.c_size_t(16),
+                              ctypes.c_int64(64), ctypes.c_int64(1152), 0, 0, stream())
+    assert rc == 4
+
+
+def test_compile_fullgraph():
+    x, w, g = (t.to(dev) for t in O.rmsnorm_inputs(256, 1152, torch.float32, seed=4))
+    fn = torch.compile(lambda a, b: krsi().rmsnorm(a, b, 1e-6), fullgraph=True)
+    xr = x.clone().requires_grad_(True)
+    out = fn(xr, w)
+    (gx,) = torch.autograd.grad(out, [xr], g)
+    y, r = torch.ops.krsi.rmsnorm_fwd(x, w, 1e-6)
+    dx, _ = torch.ops.krsi.rmsnorm_bwd(g, x, w, r)
+    assert torch.equal(out, y) and torch.equal(gx, dx)
