@@ -1,8 +1,407 @@
-// placeholder replaced by the tcgen05 forward kernel
+// relpos_attn_fwd.cu - relative-position-bias flash attention forward for B200 (sm_100a).
+//
+// Computes what library/relpos_attention.py:26-59 (_fwd) computes, for every (b, h):
+//   s2[i, j] = (q_i . k_j * scale + pd[h, j - i + S - 1]) * log2(e)
+//   m_i = max_j s2, l_i = sum_j exp2(s2 - m_i), out_i = sum_j exp2(s2 - m_i) v_j / l_i,
+//   lse_i = m_i + log2(l_i); out in the input dtype, out32 in fp32.
+//
+// Structure (one CTA = two 128-query tiles of one (b, h), 10 warps):
+//   warp 0      TMA producer: Q once; per 128-key block a K tile, a V tile (3-stage ring) and a
+//               slab of the 383 bias values that block needs (pre-multiplied by log2 e);
+//   warp 1      TMEM owner (512 columns) and the single-thread tcgen05.mma issuer:
+//               S_t = Q_t K^T (SS, K = DP) into TMEM, O_t += P_t V (TS: P read from TMEM);
+//   warps 2-5   softmax for query tile 0, warps 6-9 for tile 1 (one query row per thread,
+//               row = TMEM lane): S from TMEM -> bias add -> online softmax with the rescale of
+//               O skipped unless the running max grows by more than 2^8 -> P (bf16/f16) written
+//               back over S in TMEM -> at the end O / l to global memory.
+// The two query tiles ping-pong so one tile's softmax overlaps the other tile's MMAs.
+// Every wait is bounded (watchdog.cuh); a stalled pipeline ends the CTA with an error word.
+#include <string.h>
+
+#include <type_traits>
+
+#include "attn_common.cuh"
 #include "common.cuh"
 #include "watchdog.cuh"
+
 KRSI_DEFINE_WATCHDOG(attn_fwd)
-extern "C" int krsi_relpos_attn_fwd(const void*, int64_t, const float*, void*, float*, float*, int64_t, int64_t,
-                                    int64_t, int64_t, float, int, cudaStream_t) {
-  return KRSI_ERR_UNSUPPORTED;
+
+namespace krsi {
+namespace {
+
+using namespace sm100;
+using attn::DLayout;
+using attn::kTileRows;
+
+constexpr int kBN = 128;            // keys per block
+constexpr int kQTiles = 2;          // query tiles per CTA
+constexpr int kThreads = 320;       // 10 warps
+constexpr int kSlab = 384;          // floats per bias slab (2*128 + 128 - 1 = 383 used)
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleThreshold = 8.0f;   // log2 units: P <= 2^8 between rescales
+
+template <int DP>
+struct FwdCfg {
+  using L = DLayout<DP>;
+  static constexpr int NS = DP <= 96 ? 3 : 2;                      // K/V pipeline stages
+  static constexpr uint32_t kTile = L::tile_bytes(kTileRows);       // one 128 x DP tile
+  static constexpr uint32_t kQOff = 0;
+  static constexpr uint32_t kKVOff = kQOff + kQTiles * kTile;
+  static constexpr uint32_t kSlabOff = kKVOff + NS * 2 * kTile;
+  static constexpr uint32_t kBarOff = kSlabOff + NS * kSlab * 4;
+  static constexpr int kNumBars = 1 + 2 * NS + 3 * kQTiles + 1;     // q_full, kv_full/empty, s/p/o, drain
+  static constexpr uint32_t kMiscOff = kBarOff + kNumBars * 8;
+  static constexpr uint32_t kSmem = kMiscOff + 16 + 1024;           // + alignment slack
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kSCol = 0;                              // S_t at t*128
+  static constexpr uint32_t kOCol = 256;                            // O_t at 256 + t*DP
+  static_assert(kOCol + kQTiles * DP <= kTmemCols, "TMEM budget");
+};
+
+struct FwdArgs {
+  const float* pd;
+  void* out;
+  float* out32;
+  float* lse;
+  int B, S, H, D;
+  float scale_log2;   // scale * log2(e)
+  int n_kb;           // key blocks
+  uint32_t spin_limit;
+};
+
+template <int DP, bool F16>
+__global__ void __launch_bounds__(kThreads, 1)
+relpos_fwd_kernel(const __grid_constant__ CUtensorMap m64, const __grid_constant__ CUtensorMap m32,
+                  const __grid_constant__ CUtensorMap m16, const FwdArgs a) {
+  using C = FwdCfg<DP>;
+  using L = DLayout<DP>;
+  constexpr int NS = C::NS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = bars + 1 + NS;
+  uint64_t* s_ready = bars + 1 + 2 * NS;
+  uint64_t* p_ready = s_ready + kQTiles;
+  uint64_t* o_final = p_ready + kQTiles;
+  uint64_t* drain = o_final + kQTiles;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
+  float* slabs = reinterpret_cast<float*>(smem + C::kSlabOff);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
+  const int q0 = blockIdx.x * (kQTiles * kTileRows);
+  const int n_kb = a.n_kb;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&kv_full[s], 2);     // TMA expect_tx arrival + bias-slab arrival
+      mbar_init(&kv_empty[s], 1);    // tcgen05.commit
+    }
+    for (int t = 0; t < kQTiles; ++t) {
+      mbar_init(&s_ready[t], 1);
+      mbar_init(&p_ready[t], 128);
+      mbar_init(&o_final[t], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&m64);
+    prefetch_tensormap(&m32);
+    prefetch_tensormap(&m16);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, kQTiles * C::kTile);
+      for (int t = 0; t < kQTiles; ++t)
+        attn::load_tile<DP>(smem + C::kQOff + t * C::kTile, &m64, &m32, &m16, q_full, h, q0 + t * kTileRows, b);
+    }
+    const int two_s = 2 * a.S - 1;
+    const float* pdh = a.pd + (size_t)h * two_s;
+    for (int j = 0; j < n_kb; ++j) {
+      const int s = j % NS;
+      if (j >= NS && !mbar_wait_bounded(&kv_empty[s], ((j / NS) + 1) & 1, abort_flag, a.spin_limit)) {
+        watchdog_fire(kWdFwdLoad);
+        break;
+      }
+      uint8_t* kt = smem + C::kKVOff + (2 * s) * C::kTile;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&kv_full[s], 2 * C::kTile);
+        attn::load_tile<DP>(kt, &m64, &m32, &m16, &kv_full[s], a.H + h, j * kBN, b);
+        attn::load_tile<DP>(kt + C::kTile, &m64, &m32, &m16, &kv_full[s], 2 * a.H + h, j * kBN, b);
+      }
+      // bias slab: slab[idx] = pd[h, j*128 - q0 - 255 + idx + S - 1] * log2e, zero outside the table
+      float* slab = slabs + s * kSlab;
+      const int base = j * kBN - q0 - (kQTiles * kTileRows - 1) + a.S - 1;
+      for (int idx = lane; idx < kSlab; idx += 32) {
+        const int pos = base + idx;
+        slab[idx] = (pos >= 0 && pos < two_s) ? __ldg(pdh + pos) * kLog2e : 0.f;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&kv_full[s]);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t fmt = F16 ? 0u : 1u;
+      constexpr uint32_t id_qk = idesc_f16(128, kBN, fmt, false, false);
+      const uint32_t q_addr = smem_u32(smem + C::kQOff);
+      const uint32_t kv_addr = smem_u32(smem + C::kKVOff);
+      bool ok = mbar_wait_bounded(q_full, 0, abort_flag, a.spin_limit) &&
+                mbar_wait_bounded(&kv_full[0], 0, abort_flag, a.spin_limit);
+      auto issue_qk = [&](int t, int j) {
+        const uint32_t kt = kv_addr + (2 * (j % NS)) * C::kTile;
+#pragma unroll
+        for (int kk = 0; kk < DP / 16; ++kk) {
+          const uint64_t ad = attn::kmajor_desc<DP>(q_addr + t * C::kTile, kTileRows, kk * 16);
+          const uint64_t bd = attn::kmajor_desc<DP>(kt, kTileRows, kk * 16);
+          mma_ss(tmem + C::kSCol + t * kBN, ad, bd, id_qk, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t vt = kv_addr + (2 * (j % NS) + 1) * C::kTile;
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint32_t a_tmem = tmem + C::kSCol + t * kBN + kk * 8;   // P: 2 x 16-bit per column
+#pragma unroll
+          for (int c = 0; c < L::NCHUNK; ++c) {
+            const uint32_t id_pv = idesc_f16(128, L::width(c), fmt, false, true);
+            const uint64_t bd = attn::mnmajor_desc<DP>(vt, kTileRows, c, kk * 16);
+            mma_ts(tmem + C::kOCol + t * DP + L::start(c), a_tmem, bd, id_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+      };
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < kQTiles; ++t) {
+          issue_qk(t, 0);
+          mma_commit(&s_ready[t]);
+        }
+        for (int j = 0; j < n_kb && ok; ++j) {
+          const bool has_next = j + 1 < n_kb;
+          if (has_next && !mbar_wait_bounded(&kv_full[(j + 1) % NS], ((j + 1) / NS) & 1, abort_flag, a.spin_limit)) {
+            ok = false;
+            break;
+          }
+          for (int t = 0; t < kQTiles; ++t) {
+            if (!mbar_wait_bounded(&p_ready[t], j & 1, abort_flag, a.spin_limit)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(t, j);
+            if (has_next) {
+              issue_qk(t, j + 1);
+              mma_commit(&s_ready[t]);
+            } else {
+              mma_commit(&o_final[t]);
+            }
+          }
+          if (!ok) break;
+          mma_commit(&kv_empty[j % NS]);
+        }
+      }
+      if (!ok) watchdog_fire(kWdFwdMma);
+      // Drain: every MMA issued above has completed before TMEM is released.
+      mma_commit(drain);
+      for (uint32_t i = 0; i < a.spin_limit && !mbar_try_wait(drain, 0); ++i) {
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax (warps 2..9)
+    const int t = (warp - 2) / 4;                       // query tile
+    const int quarter = warp % 4;                       // TMEM lane quarter of this warp
+    const int r = quarter * 32 + lane;                  // row within the tile
+    const int q = q0 + t * kTileRows + r;               // query index within the sequence
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    const uint32_t s_tmem = tmem + lane_addr + C::kSCol + t * kBN;
+    const uint32_t o_tmem = tmem + lane_addr + C::kOCol + t * DP;
+    const int slab_base = (kQTiles - 1 - t) * kTileRows + (kTileRows - 1) - r;   // slab[slab_base + c]
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kb; ++j) {
+      const int s = j % NS;
+      if (!mbar_wait_bounded(&s_ready[t], j & 1, abort_flag, a.spin_limit) ||
+          !mbar_wait_bounded(&kv_full[s], (j / NS) & 1, abort_flag, a.spin_limit)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sv[kBN];
+      {
+        uint32_t* u = reinterpret_cast<uint32_t*>(sv);
+#pragma unroll
+        for (int c = 0; c < kBN; c += 32) tmem_ld32(s_tmem + c, u + c);
+        tmem_wait_ld();
+      }
+      const float* slab = slabs + s * kSlab + slab_base;
+      const int valid = a.S - j * kBN;                  // keys of this block inside the sequence
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kBN; ++c) {
+        float v = fmaf(sv[c], a.scale_log2, slab[c]);
+        v = c < valid ? v : -INFINITY;
+        sv[c] = v;
+        mx = fmaxf(mx, v);
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const bool need = m_new - m_run > kRescaleThreshold;   // true on the first block (m_run = -inf)
+      float alpha = 1.f, m_use = m_run;
+      const bool warp_rescale = __any_sync(0xffffffffu, need);
+      if (warp_rescale) {
+        m_use = m_new;
+        alpha = ex2_approx(m_run - m_new);              // 0 on the first block
+      }
+      float sum = 0.f;
+      uint32_t pk[kBN / 2];
+#pragma unroll
+      for (int c = 0; c < kBN; c += 2) {
+        const float p0 = ex2_approx(sv[c] - m_use);
+        const float p1 = ex2_approx(sv[c + 1] - m_use);
+        sum += p0 + p1;
+        pk[c / 2] = F16 ? pack_f16x2(p0, p1) : pack_bf16x2(p0, p1);
+      }
+      l_run = l_run * alpha + sum;
+      m_run = m_use;
+      tmem_st32(s_tmem, pk);
+      tmem_st32(s_tmem + 32, pk + 32);
+      if (warp_rescale && j > 0) {
+        // O_t holds the sum through block j-1 (PV(t, j-1) completed before S_t(j) was ready).
+#pragma unroll
+        for (int c = 0; c < DP; c += 16) {
+          uint32_t ov[16];
+          tmem_ld16(o_tmem + c, ov);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+          tmem_st16(o_tmem + c, ov);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_ready[t]);
+    }
+    if (ok && !mbar_wait_bounded(&o_final[t], 0, abort_flag, a.spin_limit)) ok = false;
+    if (!ok) {
+      watchdog_fire(kWdFwdSoftmax);
+    } else {
+      tc_fence_after();
+      // All lanes run the warp-collective TMEM loads; rows past the sequence end skip the stores.
+      const bool row_ok = q < a.S;
+      const float inv_l = 1.0f / l_run;
+      const size_t row = (size_t)b * a.S + (row_ok ? q : 0);
+      const size_t ld = (size_t)a.H * a.D;
+      float* o32 = a.out32 + row * ld + (size_t)h * a.D;
+      using T = typename std::conditional<F16, __half, __nv_bfloat16>::type;
+      T* o16 = reinterpret_cast<T*>(a.out) + row * ld + (size_t)h * a.D;
+#pragma unroll
+      for (int c = 0; c < DP; c += 16) {
+        uint32_t ov[16];
+        tmem_ld16(o_tmem + c, ov);
+        tmem_wait_ld();
+        float f[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) f[e] = __uint_as_float(ov[e]) * inv_l;
+#pragma unroll
+        for (int e = 0; e < 16; e += 8) {
+          if (row_ok && c + e < a.D) {   // D is a multiple of 8: whole 8-column groups are in or out
+            float4* d32 = reinterpret_cast<float4*>(o32 + c + e);
+            d32[0] = make_float4(f[e], f[e + 1], f[e + 2], f[e + 3]);
+            d32[1] = make_float4(f[e + 4], f[e + 5], f[e + 6], f[e + 7]);
+            uint4 pk;
+            if (F16) {
+              pk = make_uint4(pack_f16x2(f[e], f[e + 1]), pack_f16x2(f[e + 2], f[e + 3]),
+                              pack_f16x2(f[e + 4], f[e + 5]), pack_f16x2(f[e + 6], f[e + 7]));
+            } else {
+              pk = make_uint4(pack_bf16x2(f[e], f[e + 1]), pack_bf16x2(f[e + 2], f[e + 3]),
+                              pack_bf16x2(f[e + 4], f[e + 5]), pack_bf16x2(f[e + 6], f[e + 7]));
+            }
+            *reinterpret_cast<uint4*>(o16 + c + e) = pk;
+          }
+        }
+      }
+      if (row_ok) a.lse[(size_t)bh * a.S + q] = m_run + __log2f(l_run);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
+}
+
+template <int DP, bool F16>
+int launch_fwd(const attn::HeadMaps& hm, const FwdArgs& a, cudaStream_t stream) {
+  using C = FwdCfg<DP>;
+  auto kern = relpos_fwd_kernel<DP, F16>;
+  KRSI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem));
+  dim3 grid((a.S + kQTiles * kTileRows - 1) / (kQTiles * kTileRows), a.B * a.H);
+  kern<<<grid, kThreads, C::kSmem, stream>>>(hm.m64, hm.m32, hm.m16, a);
+  KRSI_LAUNCH_CHECK();
+  return KRSI_OK;
+}
+
+template <bool F16>
+int dispatch_dp(int DP, const attn::HeadMaps& hm, const FwdArgs& a, cudaStream_t s) {
+  switch (DP) {
+    case 32: return launch_fwd<32, F16>(hm, a, s);
+    case 64: return launch_fwd<64, F16>(hm, a, s);
+    case 80: return launch_fwd<80, F16>(hm, a, s);
+    case 96: return launch_fwd<96, F16>(hm, a, s);
+    case 128: return launch_fwd<128, F16>(hm, a, s);
+    default: return KRSI_ERR_UNSUPPORTED;
+  }
+}
+
+}  // namespace
+
+// Padded head width used by both attention kernels (compiled variants: 32, 64, 80, 96, 128).
+int attn_padded_dim(int64_t D) {
+  if (D <= 0 || D > 128 || D % 8 != 0) return -1;
+  const int dp = (int)((D + 15) / 16 * 16);
+  if (dp <= 32) return 32;
+  if (dp <= 64) return 64;
+  if (dp <= 80) return 80;
+  if (dp <= 96) return 96;
+  return 128;
+}
+
+}  // namespace krsi
+
+using namespace krsi;
+
+extern "C" int krsi_relpos_attn_fwd(const void* qkv, int64_t qkv_row_stride, const float* pd, void* out,
+                                    float* out32, float* lse, int64_t B, int64_t S, int64_t H, int64_t D,
+                                    float scale, int dtype, cudaStream_t stream) {
+  KRSI_CHECK_ARG(B >= 0 && S >= 0 && H > 0 && D > 0);
+  if (B == 0 || S == 0) return KRSI_OK;
+  KRSI_CHECK_ARG(qkv && pd && out && out32 && lse);
+  if (dtype != KRSI_BF16 && dtype != KRSI_F16) return KRSI_ERR_UNSUPPORTED;
+  const int DP = attn_padded_dim(D);
+  if (DP < 0) return KRSI_ERR_UNSUPPORTED;
+  KRSI_CHECK_ARG(qkv_row_stride >= 3 * H * D);
+  if (qkv_row_stride % 8 != 0 || !aligned16(qkv) || !aligned16(out) || !aligned16(out32))
+    return KRSI_ERR_MISALIGNED;
+  if (S > (1 << 24) || B * H > 65535) return KRSI_ERR_UNSUPPORTED;
+  attn::HeadMaps hm;
+  if (!attn::make_head_maps(&hm, DP, qkv, qkv_row_stride, B, S, 3 * H, D, dtype == KRSI_F16))
+    return KRSI_ERR_CUDA;
+  FwdArgs a{pd, out, out32, lse, (int)B, (int)S, (int)H, (int)D, scale * 1.4426950408889634f,
+            (int)((S + kBN - 1) / kBN), kSpinLimit};
+  return dtype == KRSI_F16 ? dispatch_dp<true>(DP, hm, a, stream) : dispatch_dp<false>(DP, hm, a, stream);
 }

@@ -200,24 +200,54 @@ rms_bwd_kernel(const typename Elem<XT>::T* __restrict__ g, const typename Elem<X
 }
 
 // Stage 2 of dw: dw[col] = sum over the partial rows in a fixed order, rounded to w's dtype.
-// A block covers 32 columns with 8 warps; warp i sums partial rows i, i+8, ...; the eight
-// warp sums are then added in index order.
+// A block covers 128 columns (one float4 per lane) with 16 warps; warp i sums partial rows
+// i, i+16, ... with its loads issued 8 at a time, then the 16 warp sums are added in index
+// order.  The order depends only on the partial count, so dw is bitwise reproducible.
+constexpr int kRedWarps = 16;
 template <int WT>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kRedWarps * 32)
 rms_dw_reduce_kernel(const float* __restrict__ part, typename Elem<WT>::T* __restrict__ dw, int nparts, int n) {
-  __shared__ float acc[8][33];
+  __shared__ float4 acc[kRedWarps][32];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int col = blockIdx.x * 32 + lane;
-  float s = 0.f;
-  if (col < n)
-    for (int p = wid; p < nparts; p += 8) s += part[(int64_t)p * n + col];
+  const int col = (blockIdx.x * 32 + lane) * 4;
+  const bool vec = (n % 4) == 0;
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (col < n) {
+    for (int p0 = wid; p0 < nparts; p0 += 8 * kRedWarps) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int p = p0 + u * kRedWarps;
+        const float* src = part + (int64_t)p * n + col;
+        if (p >= nparts) {
+          v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        } else if (vec) {
+          v[u] = __ldg(reinterpret_cast<const float4*>(src));
+        } else {
+          v[u].x = __ldg(src);
+          v[u].y = col + 1 < n ? __ldg(src + 1) : 0.f;
+          v[u].z = col + 2 < n ? __ldg(src + 2) : 0.f;
+          v[u].w = col + 3 < n ? __ldg(src + 3) : 0.f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        s.x += v[u].x; s.y += v[u].y; s.z += v[u].z; s.w += v[u].w;
+      }
+    }
+  }
   acc[wid][lane] = s;
   __syncthreads();
   if (wid == 0 && col < n) {
-    float tsum = 0.f;
+    float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) tsum += acc[i][lane];
-    dw[col] = Elem<WT>::store(tsum);
+    for (int i = 0; i < kRedWarps; ++i) {
+      t.x += acc[i][lane].x; t.y += acc[i][lane].y; t.z += acc[i][lane].z; t.w += acc[i][lane].w;
+    }
+    const float tv[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      if (col + e < n) dw[col + e] = Elem<WT>::store(tv[e]);
   }
 }
 
@@ -282,8 +312,8 @@ int run_bwd(const BwdArgs& a) {
       (const typename Elem<XT>::T*)a.g, (const typename Elem<XT>::T*)a.x, (const typename Elem<WT>::T*)a.w,
       a.rstd, (typename Elem<XT>::T*)a.dx, a.part, a.rows, a.n);
   KRSI_LAUNCH_CHECK();
-  rms_dw_reduce_kernel<WT><<<(unsigned)((a.n + 31) / 32), 256, 0, a.s>>>(a.part, (typename Elem<WT>::T*)a.dw,
-                                                                         (int)a.nblocks, a.n);
+  rms_dw_reduce_kernel<WT><<<(unsigned)((a.n + 127) / 128), kRedWarps * 32, 0, a.s>>>(
+      a.part, (typename Elem<WT>::T*)a.dw, (int)a.nblocks, a.n);
   KRSI_LAUNCH_CHECK();
   return KRSI_OK;
 }

@@ -3,6 +3,7 @@ import ctypes
 
 import torch
 
+import _ext  # noqa: F401  (loads the native libraries: registers the krsi::* operators)
 from conftest import PKG
 
 DT = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
