@@ -264,7 +264,156 @@ class GegluWorkload(RMSNormWorkload):
         return self.work, "one full fwd+bwd of config 2 (reference torch path, fp32 on CPU)"
 
 
-WORKLOADS = {"rmsnorm": RMSNormWorkload, "geglu": GegluWorkload}
+class AttnWorkload(OpWorkload):
+    """Config 4: relpos attention fwd+bwd, B=8 H=16 L=2048 D=72 bf16 (training mode).  Forward and
+    backward are captured as separate CUDA graphs so the backward (the dominant kernel) is timed on
+    its own with CUDA events."""
+    name, metric, unit, dtype = "attn", "relpos attention fwd+bwd throughput", "TFLOP/s", "bf16"
+    B, S, H, D = 8, 2048, 16, 72
+    fwd_only = False
+
+    @property
+    def work(self):
+        return (4 if self.fwd_only else 12) * self.B * self.H * self.S ** 2 * self.D
+
+    @property
+    def in_bytes(self):
+        return self.B * self.S * self.H * self.D * 2 * (3 if self.fwd_only else 4)
+
+    launches_per_step = 5   # fwd; bwd prep, main, dq, dpd
+    kernel_key = "relpos_bwd_main_kernel"
+
+    def config(self):
+        return {"workload": f"relpos attention {'fwd' if self.fwd_only else 'fwd+bwd'} bf16 "
+                            f"B={self.B} H={self.H} L={self.S} D={self.D}", "flop_convention":
+                "4*B*H*L^2*D fwd, 8*B*H*L^2*D bwd (D=72 counted, not the padded 80; bwd recompute not counted)",
+                "l2": "rotating input copies > L2", "timing": "CUDA graphs (fwd, bwd)"}
+
+    def setup_host(self):
+        from oracle import ops as O
+
+        self.host = O.attn_inputs(self.B, self.S, self.H, self.D, torch.bfloat16, seed=0)
+        self.scale = self.D ** -0.5
+
+    def setup(self, dev):
+        self.setup_host()
+        self.copies = max(2, math.ceil(3 * L2_BYTES / max(self.in_bytes, 1)))
+        self.dev_inputs = [tuple(t.to(dev) for t in self.host) for _ in range(self.copies)]
+        self.pinned = tuple(t.pin_memory() for t in self.host)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for inp in self.dev_inputs:
+                self.run_fwd(*inp)
+                if not self.fwd_only:
+                    self.run_bwd(*inp)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        self.fwd_graphs, self.bwd_graphs = [], []
+        for inp in self.dev_inputs:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.run_fwd(*inp)
+            self.fwd_graphs.append(g)
+            if not self.fwd_only:
+                g2 = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g2):
+                    self.run_bwd(*inp)
+                self.bwd_graphs.append(g2)
+        self.i = 0
+        self.bwd_ms, self.fwd_ms = [], []
+
+    def run_fwd(self, qkv, pd, dout):
+        self.saved = torch.ops.krsi.relpos_attn_fwd(qkv, pd, self.B, self.S, self.H, self.D, self.scale)
+        return self.saved
+
+    def run_bwd(self, qkv, pd, dout):
+        _, out32, lse = self.saved
+        return torch.ops.krsi.relpos_attn_bwd(dout, qkv, pd, out32, lse, self.B, self.S, self.H, self.D, self.scale)
+
+    def step(self, timed=None):
+        k = self.i % self.copies
+        self.i += 1
+        if timed is None:
+            self.fwd_graphs[k].replay()
+            if not self.fwd_only:
+                self.bwd_graphs[k].replay()
+            return
+        mid = torch.cuda.Event(enable_timing=True)
+        timed[0].record()
+        self.fwd_graphs[k].replay()
+        mid.record()
+        if not self.fwd_only:
+            self.bwd_graphs[k].replay()
+        timed[1].record()
+        self._pending = (timed[0], mid, timed[1])
+        self.events = getattr(self, "events", []) + [self._pending]
+
+    def roofline(self, kms, pk):
+        fwd = [a.elapsed_time(m) for a, m, _ in self.events]
+        bwd = [m.elapsed_time(b) for _, m, b in self.events]
+        self.fwd_ms, self.bwd_ms = fwd, bwd
+        if self.fwd_only:
+            t, flop, key = statistics.median(fwd), self.work, "relpos_fwd_kernel"
+        else:
+            t, flop, key = statistics.median(bwd), 8 * self.B * self.H * self.S ** 2 * self.D, "relpos_bwd (4 kernels)"
+        ach = flop / (t / 1e3) / 1e12
+        return {"bound": "tensor", "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": ach / pk["bf16_tflops"], "traffic": ncu_traffic(key), "kernel": key,
+                "peak_source": pk["source"] + " (burst bf16 cuBLAS)"}
+
+    def extra(self):
+        f = statistics.median(self.fwd_ms) if self.fwd_ms else None
+        b = statistics.median(self.bwd_ms) if self.bwd_ms else None
+        d = {"fwd_ms": f}
+        if not self.fwd_only:
+            d.update(bwd_ms=b, fwd_tflops=4 * self.B * self.H * self.S ** 2 * self.D / (f / 1e3) / 1e12,
+                     bwd_tflops=8 * self.B * self.H * self.S ** 2 * self.D / (b / 1e3) / 1e12,
+                     fwd_bwd_tflops_14bhl2d=14 * self.B * self.H * self.S ** 2 * self.D / ((f + b) / 1e3) / 1e12)
+        return {"breakdown": d}
+
+    def e2e_step(self, dev):
+        import relpos_attention as ra
+
+        qkv, pd, dout = (t.to(dev, non_blocking=True) for t in self.pinned)
+        q, p = qkv.requires_grad_(True), pd.requires_grad_(True)
+        out = ra.relpos_attention(q, p, self.B, self.S, self.H, self.D, self.scale)
+        if self.fwd_only:
+            res = [out.detach().to("cpu")]
+        else:
+            dq, dp = torch.autograd.grad(out, [q, p], dout)
+            res = [out.detach().to("cpu"), dq.to("cpu"), dp.to("cpu")]
+        h2d = sum(t.numel() * t.element_size() for t in (self.pinned if not self.fwd_only else self.pinned[:2]))
+        return res, h2d, sum(t.numel() * t.element_size() for t in res)
+
+    def cpu_sample(self):
+        """One batch element (B=1) of the config on the reference's torch path in fp32 (the math
+        backend SDPA); work is counted for that batch element only."""
+        from oracle import ops as O
+
+        B1 = 1
+        qkv, pd, dout = (t[: B1 * self.S] if t.dim() == 2 and t.shape[0] == self.B * self.S else t for t in self.host)
+        q = qkv.float().clone().requires_grad_(True)
+        p = pd.clone().requires_grad_(True)
+        out = O.relpos_reference(q, p, B1, self.S, self.H, self.D, self.scale)
+        if not self.fwd_only:
+            torch.autograd.grad(out, [q, p], dout.float())
+        flop = (4 if self.fwd_only else 12) * B1 * self.H * self.S ** 2 * self.D
+        return flop, (f"B=1 slice of the config ({'fwd' if self.fwd_only else 'fwd+bwd'}), reference torch "
+                      "fp32 math-SDPA path")
+
+
+class AttnFwdWorkload(AttnWorkload):
+    """Config 3: relpos attention forward, B=2 H=16 L=1024 D=72 bf16."""
+    name, metric = "attn_fwd", "relpos attention fwd throughput"
+    B, S, H, D = 2, 1024, 16, 72
+    fwd_only = True
+    launches_per_step = 1
+    kernel_key = "relpos_fwd_kernel"
+
+
+WORKLOADS = {"rmsnorm": RMSNormWorkload, "geglu": GegluWorkload, "attn": AttnWorkload,
+             "attn_fwd": AttnFwdWorkload}
 
 
 def load_workloads():

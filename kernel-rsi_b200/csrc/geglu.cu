@@ -27,9 +27,10 @@ struct GeluParts {
 
 __device__ __forceinline__ GeluParts gelu_parts(float a) {
   const float z = kSqrt2OverPi * (a + kGeluC * a * a * a);
-  // exp(2z) on the SFU; 1 - 2/(e+1) saturates to +-1 for large |z| (e = inf or 0).
-  const float e = ex2_approx(2.0f * z * kLog2e);
-  const float t = 1.0f - 2.0f / (e + 1.0f);
+  // exp(2z) and the reciprocal on the SFU (the reference's tl.exp and approximate division);
+  // 1 - 2/(e+1) saturates to +-1 for large |z| (e = inf or 0).
+  const float e = ex2_approx(2.0f * kLog2e * z);
+  const float t = fmaf(-2.0f, rcp_approx(e + 1.0f), 1.0f);
   return {t, 0.5f * a * (1.0f + t)};
 }
 
