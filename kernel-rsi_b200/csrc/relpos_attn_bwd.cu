@@ -136,7 +136,8 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap q64, const __grid_con
     mbar_init(dq_free, 128);
     mbar_init(kdv_done, 1);
     mbar_init(drain, 1);
-    *abort_flag = 0;
+    abort_flag[0] = 0;
+    abort_flag[1] = 0;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -275,12 +276,17 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap q64, const __grid_con
     const uint32_t dpt_t = tmem + lane_addr + C::kDPT;
     uint8_t* ds_smem = smem + C::kDSOff;
     float* scan = reinterpret_cast<float*>(smem + C::kScanOff) + (warp - 2) * 160;
+    volatile int* wg_fail = abort_flag + 1;   // written only before the first named barrier below
     bool ok = true;
     for (int i = 0; i < nq; ++i) {
       const int s = i % NQS;
       const int q0 = i * kBlk;
-      if (!mbar_wait_bounded(sdp_ready, i & 1, abort_flag, a.spin_limit) ||
-          !mbar_wait_bounded(&qdo_full[s], (i / NQS) & 1, abort_flag, a.spin_limit)) {
+      const bool w_ok = mbar_wait_bounded(sdp_ready, i & 1, abort_flag, a.spin_limit) &&
+                        mbar_wait_bounded(&qdo_full[s], (i / NQS) & 1, abort_flag, a.spin_limit);
+      // All 128 threads take the same branch: warp-collective TMEM ops and named barriers follow.
+      if (!__all_sync(0xffffffffu, w_ok) && lane == 0) *wg_fail = 1;
+      named_bar(1, 128);
+      if (*wg_fail) {
         ok = false;
         break;
       }
@@ -381,7 +387,7 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap q64, const __grid_con
     const uint32_t dq_t = tmem + lane_addr + C::kDQ;
     bool ok = true;
     for (int i = 0; i < nq; ++i) {
-      if (!mbar_wait_bounded(dq_ready, i & 1, abort_flag, a.spin_limit)) {
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(dq_ready, i & 1, abort_flag, a.spin_limit))) {
         ok = false;
         break;
       }
@@ -404,7 +410,7 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap q64, const __grid_con
       }
     }
     // dK, dV (rows = keys) -> dqkv
-    if (ok && !mbar_wait_bounded(kdv_done, 0, abort_flag, a.spin_limit)) ok = false;
+    if (ok && !__all_sync(0xffffffffu, mbar_wait_bounded(kdv_done, 0, abort_flag, a.spin_limit))) ok = false;
     if (!ok) {
       watchdog_fire(kWdBwdDq);
     } else {

@@ -236,8 +236,9 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap m64, const __grid_constant
     bool ok = true;
     for (int j = 0; j < n_kb; ++j) {
       const int s = j % NS;
-      if (!mbar_wait_bounded(&s_ready[t], j & 1, abort_flag, a.spin_limit) ||
-          !mbar_wait_bounded(&kv_full[s], (j / NS) & 1, abort_flag, a.spin_limit)) {
+      const bool w_ok = mbar_wait_bounded(&s_ready[t], j & 1, abort_flag, a.spin_limit) &&
+                        mbar_wait_bounded(&kv_full[s], (j / NS) & 1, abort_flag, a.spin_limit);
+      if (!__all_sync(0xffffffffu, w_ok)) {   // warp-uniform: TMEM loads/stores are warp-collective
         ok = false;
         break;
       }
@@ -296,7 +297,7 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap m64, const __grid_constant
       tc_fence_before();
       mbar_arrive(&p_ready[t]);
     }
-    if (ok && !mbar_wait_bounded(&o_final[t], 0, abort_flag, a.spin_limit)) ok = false;
+    if (ok && !__all_sync(0xffffffffu, mbar_wait_bounded(&o_final[t], 0, abort_flag, a.spin_limit))) ok = false;
     if (!ok) {
       watchdog_fire(kWdFwdSoftmax);
     } else {
