@@ -412,8 +412,141 @@ class AttnFwdWorkload(AttnWorkload):
     kernel_key = "relpos_fwd_kernel"
 
 
+class TimedAttention(torch.autograd.Function):
+    """relpos_attention with CUDA events around its forward and backward kernels (same ops as the
+    library's RelPosAttention), so the block step can report the attention roofline live."""
+    log = None
+
+    @staticmethod
+    def forward(ctx, qkv, pd, B, S, H, D, scale):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        out, out32, lse = torch.ops.krsi.relpos_attn_fwd(qkv, pd, B, S, H, D, scale)
+        e1.record()
+        if TimedAttention.log is not None:
+            TimedAttention.log.append(("fwd", e0, e1))
+        ctx.save_for_backward(qkv, pd, out32, lse)
+        ctx.dims = (B, S, H, D, scale)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        dqkv, dpd = torch.ops.krsi.relpos_attn_bwd(dout.contiguous(), *ctx.saved_tensors, *ctx.dims)
+        e1.record()
+        if TimedAttention.log is not None:
+            TimedAttention.log.append(("bwd", e0, e1))
+        return dqkv, dpd, None, None, None, None, None
+
+
+class BlockWorkload:
+    """Config 5: 28-layer pre-norm block stack, x [32,1024,1152] bf16, fwd+bwd, loss =
+    mean(out.float()^2); the global batch is sharded over the ranks (strong scaling) and the only
+    collective is the layer-bucketed weight-gradient all-reduce (NCCL)."""
+    name, metric, unit, dtype = "block", "block stack fwd+bwd training throughput", "tok/s", "bf16"
+    higher_is_better = True
+    scaling = "strong"
+    GLOBAL_B = 32
+    kernel_key = "relpos_attention fwd+bwd (in block step)"
+
+    def __init__(self, rank, world):
+        import harness.block as hb
+
+        self.rank, self.world = rank, world
+        self.cfg = hb.BlockConfig()
+        self.tokens_per_step = self.GLOBAL_B * self.cfg.seq // world      # this rank's tokens
+        self.work = self.cfg.flops_per_token() * self.GLOBAL_B * self.cfg.seq
+        self.launches_per_step = self.cfg.layers * 13   # rmsnorm 2x(1+2), attn 1+4, geglu 1+1
+
+    def config(self):
+        c = self.cfg
+        return {"workload": "block stack (config 5) fwd+bwd", "layers": c.layers, "global_batch": self.GLOBAL_B,
+                "seq_len": c.seq, "d_model": c.d, "heads": c.heads, "head_dim": c.head_dim, "ffn": c.ffn,
+                "parallelism": f"dp{self.world} (batch-sharded, NCCL grad all-reduce)",
+                "flop_per_step": self.work, "l2": "inputs and activations >> L2",
+                "timing": "eager autograd (CUDA events)"}
+
+    def setup_host(self):
+        g = torch.Generator().manual_seed(0)
+        self.x_global = torch.randn(self.GLOBAL_B, self.cfg.seq, self.cfg.d, generator=g).to(torch.bfloat16)
+
+    def setup(self, dev):
+        import harness.block as hb
+        from harness.grad_sync import LayerBucketAllReduce, shard_batch
+
+        self.setup_host()
+        ops = hb.LibraryOps()
+        ops.relpos_attention = TimedAttention.apply
+        self.model = hb.BlockStack(self.cfg, ops, dev, seed=0)
+        self.reducer = LayerBucketAllReduce(self.model.layers)
+        x = shard_batch(self.x_global, self.rank, self.world)
+        self.x = x.to(dev)
+        self.x_pinned = x.contiguous().pin_memory()
+        self.events = []
+        self.loss_fn = hb.loss_fn
+
+    def step(self, timed=None):
+        from harness.grad_sync import train_step
+
+        TimedAttention.log = [] if timed is not None else None
+        if timed is not None:
+            timed[0].record()
+        loss = train_step(self.model, self.x, self.reducer, self.world, self.loss_fn)
+        if timed is not None:
+            timed[1].record()
+            self.events.append(TimedAttention.log)
+        TimedAttention.log = None
+        return loss
+
+    def roofline(self, kms, pk):
+        per_step = [sum(a.elapsed_time(b) for _, a, b in log) for log in self.events]
+        fwd = [sum(a.elapsed_time(b) for k, a, b in log if k == "fwd") for log in self.events]
+        t = statistics.median(per_step)
+        c = self.cfg
+        B_local = self.GLOBAL_B // self.world
+        flop = 12 * B_local * c.heads * c.seq ** 2 * c.head_dim * c.layers
+        ach = flop / (t / 1e3) / 1e12
+        self._attn = {"attn_ms_per_step": t, "attn_fwd_ms_per_step": statistics.median(fwd),
+                      "attn_share_of_step": t / kms if kms else None}
+        return {"bound": "tensor", "achieved": ach, "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                "frac": ach / pk["bf16_tflops_sustained"], "traffic": ncu_traffic("relpos_bwd_main_kernel"),
+                "kernel": self.kernel_key, "peak_source": pk["source"] + " (sustained bf16 cuBLAS: timed inside a long step)"}
+
+    def extra(self):
+        return {"breakdown": getattr(self, "_attn", {}),
+                "model_tflops": self.work / (self._step_ms / 1e3) / 1e12 if getattr(self, "_step_ms", None) else None}
+
+    def e2e_step(self, dev):
+        from harness.grad_sync import train_step
+
+        x = self.x_pinned.to(dev, non_blocking=True)
+        loss = train_step(self.model, x, self.reducer, self.world, self.loss_fn)
+        val = loss.item()                 # device -> host read of the step's result
+        return [val], self.x_pinned.numel() * 2, 4
+
+    def cpu_sample(self):
+        """One layer at B=1 (1024 tokens) fwd+bwd on the reference's torch path in fp32; reported
+        as tokens through the full 28-layer stack per second (time x 28 layers)."""
+        import harness.block as hb
+        from oracle import ops as O
+
+        class RefOps:
+            rmsnorm = staticmethod(O.rmsnorm_reference)
+            geglu = staticmethod(O.geglu_reference)
+            relpos_attention = staticmethod(O.relpos_reference)
+
+        if not hasattr(self, "_cpu_layer"):
+            cfg1 = hb.BlockConfig(layers=1)
+            self._cpu_layer = hb.BlockStack(cfg1, RefOps(), torch.device("cpu"), seed=0, dtype=torch.float32)
+        x = self.x_global[:1].float().clone().requires_grad_(True)
+        loss = hb.loss_fn(self._cpu_layer(x))
+        loss.backward()
+        return self.cfg.seq / self.cfg.layers, "1 layer, B=1 (1024 tokens) fwd+bwd fp32 reference torch path, counted as 1024/28 full-stack tokens"
+
+
 WORKLOADS = {"rmsnorm": RMSNormWorkload, "geglu": GegluWorkload, "attn": AttnWorkload,
-             "attn_fwd": AttnFwdWorkload}
+             "attn_fwd": AttnFwdWorkload, "block": BlockWorkload}
 
 
 def load_workloads():
@@ -519,6 +652,7 @@ def run_krsi_arm(args, rank, world):
     scale = 1e9 if wl.unit == "GB/s" else (1e12 if wl.unit == "TFLOP/s" else 1.0)
     per_step_work = wl.work * (world if wl.scaling == "weak" and wl.unit != "tok/s" else 1)
     value = per_step_work / (ms / 1e3) / scale if wl.unit != "tok/s" else wl.tokens_per_step * world / (ms / 1e3)
+    wl._step_ms = ms
 
     # end to end through the public API, host buffers in and results out, every step
     torch.cuda.synchronize()

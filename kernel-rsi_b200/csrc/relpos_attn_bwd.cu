@@ -275,7 +275,8 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap q64, const __grid_con
     const uint32_t st_t = tmem + lane_addr + C::kST;
     const uint32_t dpt_t = tmem + lane_addr + C::kDPT;
     uint8_t* ds_smem = smem + C::kDSOff;
-    float* scan = reinterpret_cast<float*>(smem + C::kScanOff) + (warp - 2) * 160;
+    // one scan row per lane quarter: row w holds the diagonals of keys 32w .. 32w+31
+    float* scan = reinterpret_cast<float*>(smem + C::kScanOff) + quarter * 160;
     volatile int* wg_fail = abort_flag + 1;   // written only before the first named barrier below
     bool ok = true;
     for (int i = 0; i < nq; ++i) {

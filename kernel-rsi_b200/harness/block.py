@@ -1,0 +1,104 @@
+"""The 28-layer pre-norm block stack of BASELINE config 5, built on the drop-in library ops.
+
+Each layer:  x -> RMSNorm -> fused q|k|v GEMM -> relpos attention (H heads of D) -> out GEMM -> +x
+                -> RMSNorm -> merged gate|value GEMM (d -> 2F) -> GEGLU -> down GEMM (F -> d) -> +x
+The attention, RMSNorm and GEGLU calls are the kernel-rsi library functions (relpos_attention(),
+rmsnorm(), geglu(), with the reference's signatures); the GEMMs are torch matmuls (cuBLAS).  loss =
+mean(out.float()^2).  Weights are bf16 ~ N(0, 0.02) (RMSNorm weights 1 + N(0, 0.02)), the per-layer
+relative-position table pd [H, 2L-1] is fp32 ~ N(0, 0.02).
+
+`ops` supplies the three library functions, so the same model runs on the B200 kernels or, for
+CPU tests of the distributed harness, on any stand-in with the same signatures.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+from torch import nn
+
+
+@dataclass
+class BlockConfig:
+    layers: int = 28
+    d: int = 1152
+    heads: int = 16
+    head_dim: int = 72
+    ffn: int = 4608
+    seq: int = 1024
+    eps: float = 1e-6
+
+    def params_per_layer(self) -> int:
+        return 3 * self.d * self.d + self.d * self.d + 2 * self.ffn * self.d + self.ffn * self.d
+
+    def linear_params(self) -> int:
+        return self.layers * self.params_per_layer()
+
+    def flops_per_token(self) -> int:
+        """Training FLOPs per token: 6 x linear params (GEMMs) + 12 x L x H x D x layers (attention,
+        fwd 4 + bwd 8 per query per key, D unpadded)."""
+        return 6 * self.linear_params() + 12 * self.seq * self.heads * self.head_dim * self.layers
+
+
+class Layer(nn.Module):
+    def __init__(self, cfg: BlockConfig, ops, gen: torch.Generator, device, dtype=torch.bfloat16):
+        super().__init__()
+        self.cfg, self.ops = cfg, ops
+        d, F_, H = cfg.d, cfg.ffn, cfg.heads
+
+        def w(*shape, std=0.02, mean=0.0):
+            t = torch.randn(*shape, generator=gen, device=device, dtype=torch.float32) * std + mean
+            return nn.Parameter(t.to(dtype))
+
+        self.norm1 = w(d, mean=1.0)
+        self.wqkv = w(3 * d, d)
+        self.wo = w(d, d)
+        self.norm2 = w(d, mean=1.0)
+        self.wi = w(2 * F_, d)          # rows [0, F) gate, [F, 2F) value
+        self.wo2 = w(d, F_)
+        self.pd = nn.Parameter(torch.randn(H, 2 * cfg.seq - 1, generator=gen, device=device) * 0.02)
+
+    def forward(self, x):
+        cfg, ops = self.cfg, self.ops
+        B, L, d = x.shape
+        x2 = x.reshape(B * L, d)
+        h = ops.rmsnorm(x2, self.norm1, cfg.eps)
+        qkv = h @ self.wqkv.t()
+        a = ops.relpos_attention(qkv, self.pd, B, L, cfg.heads, cfg.head_dim, 1.0 / math.sqrt(cfg.head_dim))
+        x2 = x2 + a @ self.wo.t()
+        h = ops.rmsnorm(x2, self.norm2, cfg.eps)
+        g = ops.geglu(h @ self.wi.t())
+        x2 = x2 + g @ self.wo2.t()
+        return x2.reshape(B, L, d)
+
+
+class BlockStack(nn.Module):
+    def __init__(self, cfg: BlockConfig, ops, device, seed: int = 0, dtype=torch.bfloat16):
+        super().__init__()
+        self.cfg = cfg
+        gen = torch.Generator(device=device).manual_seed(seed)
+        self.layers = nn.ModuleList(Layer(cfg, ops, gen, device, dtype) for _ in range(cfg.layers))
+
+    def forward(self, x):
+        for layer in self.layers:
+            x = layer(x)
+        return x
+
+
+def loss_fn(out: torch.Tensor) -> torch.Tensor:
+    return out.float().pow(2).mean()
+
+
+class LibraryOps:
+    """The kernel-rsi library functions (B200 kernels); imported lazily so CPU-only users of the
+    harness need not load the native extension."""
+
+    def __init__(self):
+        import geglu
+        import relpos_attention
+        import rmsnorm
+
+        self.rmsnorm = rmsnorm.rmsnorm
+        self.geglu = geglu.geglu
+        self.relpos_attention = relpos_attention.relpos_attention

@@ -1,0 +1,87 @@
+"""Weight-gradient all-reduce for the batch-sharded block harness.
+
+Each rank runs forward+backward on its own batch shard; the only collective is one SUM all-reduce
+per bucket of weight gradients (the loss is pre-scaled by 1/world, so the sum is the global-batch
+gradient).  Buckets are the layers, in reverse order: a layer's bucket is launched asynchronously
+(NCCL's own stream) the moment autograd has accumulated its last gradient, so communication of
+layer l overlaps the backward of layers l-1 ... 0.  Gradients live in one flat buffer per layer
+and dtype (param.grad are views into it), so no packing copies are needed.
+"""
+from __future__ import annotations
+
+from collections import defaultdict
+
+import torch
+import torch.distributed as dist
+
+
+class LayerBucketAllReduce:
+    def __init__(self, layers, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.buckets = []       # (layer index, dtype, flat buffer, [params])
+        self.pending = defaultdict(int)
+        self.handles = []
+        self.param_bucket = {}
+        for li, layer in enumerate(layers):
+            by_dtype = defaultdict(list)
+            for p in layer.parameters():
+                if p.requires_grad:
+                    by_dtype[p.dtype].append(p)
+            for dt, params in by_dtype.items():
+                n = sum(p.numel() for p in params)
+                flat = torch.zeros(n, dtype=dt, device=params[0].device)
+                off = 0
+                for p in params:
+                    p.grad = flat[off: off + p.numel()].view_as(p)
+                    off += p.numel()
+                    self.param_bucket[p] = len(self.buckets)
+                self.buckets.append((li, dt, flat, params))
+        self.hooks = [p.register_post_accumulate_grad_hook(self._on_grad) for p in self.param_bucket]
+
+    @property
+    def bytes(self) -> int:
+        return sum(f.numel() * f.element_size() for _, _, f, _ in self.buckets)
+
+    def zero_grad(self):
+        for _, _, flat, _ in self.buckets:
+            flat.zero_()
+        self.pending.clear()
+        self.handles.clear()
+
+    def _on_grad(self, p):
+        bi = self.param_bucket[p]
+        self.pending[bi] += 1
+        _, _, flat, params = self.buckets[bi]
+        if self.pending[bi] == len(params) and self.world > 1:
+            self.handles.append(dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group, async_op=True))
+
+    def wait(self):
+        """Make the current stream wait for every launched all-reduce (no host sync)."""
+        for h in self.handles:
+            h.wait()
+        self.handles.clear()
+
+    def remove(self):
+        for h in self.hooks:
+            h.remove()
+
+
+def shard_batch(x: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Rank r's contiguous slice of the global batch (equal shards; B divisible by world)."""
+    B = x.shape[0]
+    if B % world:
+        raise ValueError(f"global batch {B} is not divisible by world size {world}")
+    n = B // world
+    return x[rank * n: (rank + 1) * n]
+
+
+def train_step(model, x_local, reducer: LayerBucketAllReduce, world: int, loss_fn):
+    """Forward + backward on this rank's shard; returns the global-mean loss contribution of this
+    rank (loss_local / world) as a device tensor.  Gradients end as the global-batch gradient."""
+    reducer.zero_grad()
+    out = model(x_local)
+    loss = loss_fn(out) / world
+    loss.backward()
+    reducer.wait()
+    return loss.detach()

@@ -1,0 +1,128 @@
+"""The batch-sharded block harness on CPU ranks (gloo): sharding, the layer-bucket gradient
+all-reduce (N-rank averaged gradients == 1-rank full-batch gradients), and failure detection (a
+rank that dies or never joins ends the others' collectives with an error instead of a hang).
+The model runs on the oracle's reference functions (CPU stand-ins with the library signatures)."""
+import os
+import socket
+import sys
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import PKG, ROOT
+
+sys.path.insert(0, str(PKG))
+
+
+class OracleOps:
+    def __init__(self):
+        from oracle import ops as O
+        self.rmsnorm = O.rmsnorm_reference
+        self.geglu = O.geglu_reference
+        self.relpos_attention = O.relpos_reference
+
+
+def tiny_cfg():
+    from harness.block import BlockConfig
+    return BlockConfig(layers=2, d=16, heads=2, head_dim=8, ffn=24, seq=8)
+
+
+def free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def make_model(cfg):
+    from harness.block import BlockStack
+    return BlockStack(cfg, OracleOps(), torch.device("cpu"), seed=3, dtype=torch.float32)
+
+
+def global_batch(cfg, B=4):
+    g = torch.Generator().manual_seed(9)
+    return torch.randn(B, cfg.seq, cfg.d, generator=g)
+
+
+def test_shard_batch():
+    from harness.grad_sync import shard_batch
+    x = torch.arange(8).view(8, 1)
+    assert shard_batch(x, 1, 4).flatten().tolist() == [2, 3]
+    with pytest.raises(ValueError):
+        shard_batch(x, 0, 3)
+
+
+def test_config_matches_baseline_numbers():
+    from harness.block import BlockConfig
+    c = BlockConfig()
+    assert c.linear_params() == 594_542_592
+    assert c.flops_per_token() * 32 * 1024 == 129_879_811_031_040
+
+
+def _worker(rank, world, port, q, mode):
+    sys.path.insert(0, str(ROOT))
+    sys.path.insert(0, str(PKG))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.set_num_threads(1)
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+        from harness.block import loss_fn
+        from harness.grad_sync import LayerBucketAllReduce, shard_batch, train_step
+        cfg = tiny_cfg()
+        model = make_model(cfg)
+        reducer = LayerBucketAllReduce(model.layers)
+        if mode == "die" and rank == 1:
+            raise RuntimeError("planted failure on rank 1 before its first collective")
+        x = shard_batch(global_batch(cfg), rank, world)
+        loss = train_step(model, x, reducer, world, loss_fn)
+        grads = {n: p.grad.clone() for n, p in model.named_parameters()}
+        q.put((rank, "ok", float(loss), grads))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, "error", f"{type(e).__name__}: {e}", None))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def run_ranks(world, mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, mode)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = {}
+    for _ in range(world):
+        r, status, val, grads = q.get(timeout=120)
+        out[r] = (status, val, grads)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    return out
+
+
+def test_two_rank_gradients_equal_full_batch():
+    from harness.block import loss_fn
+    from harness.grad_sync import LayerBucketAllReduce, train_step
+    cfg = tiny_cfg()
+    model = make_model(cfg)
+    reducer = LayerBucketAllReduce(model.layers)   # world 1: no collective
+    loss = train_step(model, global_batch(cfg), reducer, 1, loss_fn)
+    ref = {n: p.grad.clone() for n, p in model.named_parameters()}
+    res = run_ranks(2, "ok")
+    assert all(v[0] == "ok" for v in res.values()), res
+    assert abs(res[0][1] + res[1][1] - float(loss)) < 1e-5 * max(1.0, abs(float(loss)))
+    for r in (0, 1):
+        for n, g in res[r][2].items():
+            torch.testing.assert_close(g, ref[n], rtol=1e-4, atol=1e-6)
+
+
+def test_dead_rank_raises_instead_of_hanging():
+    res = run_ranks(2, "die")
+    assert res[1][0] == "error" and "planted" in res[1][1]
+    assert res[0][0] == "error", res[0]      # its all-reduce ends with an error (peer gone / timeout)
