@@ -44,10 +44,13 @@ using attn::DLayout;
 using attn::kTileRows;
 
 constexpr int kBlk = 128;          // keys per CTA, queries per iteration
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;       // 3 warpgroups: {producer, MMA, -, -}, compute, dQ/epilogue
+constexpr uint32_t kRegsCtl = 56;   // after setmaxnreg (launch: 168 x 384 = 128 x (56 + 224 + 224))
+constexpr uint32_t kRegsWork = 224;
+constexpr int kBins = 160;          // per-warp diagonal bins: 32 keys x 128 queries -> 159 diagonals
 constexpr int kDiag = 2 * kBlk - 1;     // 255 diagonals per 128 x 128 tile
-constexpr int kDiagPad = 256;           // floats per tile vector in the workspace
-constexpr int kScan = kBlk + 31;        // diagonals one warp's 32 keys touch
+
+
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int DP>
@@ -61,8 +64,8 @@ struct BwdCfg {
   static constexpr uint32_t kDSOff = kQOff + NQS * 2 * kTile;     // dS (bf16, MN-major SW128): 2 x 16 KB
   static constexpr uint32_t kVecOff = kDSOff + 2 * 16384;         // per stage: lse[128], delta[128], slab[256]
   static constexpr uint32_t kVecBytes = (128 + 128 + 256) * 4;
-  static constexpr uint32_t kScanOff = kVecOff + NQS * kVecBytes; // 4 warps x kScan floats
-  static constexpr uint32_t kBarOff = kScanOff + 4 * 160 * 4;
+  static constexpr uint32_t kBinOff = kVecOff + NQS * kVecBytes;  // 4 warps x kBins floats
+  static constexpr uint32_t kBarOff = kBinOff + 4 * kBins * 4;
   static constexpr int kNumBars = 1 + 2 * NQS + 7;
   static constexpr uint32_t kMiscOff = kBarOff + kNumBars * 8;
   static constexpr uint32_t kSmem = kMiscOff + 16 + 1024;
@@ -76,7 +79,7 @@ struct BwdArgs {
   const float* lse;
   const float* delta;
   float* dq_acc;          // [B*S, H*D] fp32
-  float* dbias_part;      // [B*H, n_kb, n_qb, kDiagPad]
+  float* dbias_part;      // [B*H, n_kb, n_qb, 4 warps, kBins]
   void* dqkv;
   int64_t dqkv_stride;
   int B, S, H, D, n_blk;
@@ -89,8 +92,8 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
                : "memory");
 }
 
-__device__ __forceinline__ void named_bar(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+__device__ __forceinline__ void red_add_shared(uint32_t smem_addr, float v) {
+  asm volatile("red.shared.add.f32 [%0], %1;" ::"r"(smem_addr), "f"(v) : "memory");
 }
 
 template <int DP, bool F16>
@@ -153,6 +156,9 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap q64, const __grid_con
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // Each role runs entirely inside the branch that sets its register budget.
+  if (warp < 4) {
+    regs_dec<kRegsCtl>();
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
@@ -208,12 +214,12 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap q64, const __grid_con
         if (!mbar_wait_bounded(&qdo_full[s], (i / NQS) & 1, abort_flag, a.spin_limit)) { ok = false; break; }
         tc_fence_after();
         // S^T = K Q^T and dP^T = V dO^T (rows = keys)
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < DP / 16; ++kk) {
           mma_ss(tmem + C::kST, attn::kmajor_desc<DP>(k_addr, kTileRows, kk * 16),
                  attn::kmajor_desc<DP>(qt, kTileRows, kk * 16), id_sq, kk > 0);
         }
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < DP / 16; ++kk) {
           mma_ss(tmem + C::kDPT, attn::kmajor_desc<DP>(v_addr, kTileRows, kk * 16),
                  attn::kmajor_desc<DP>(dot, kTileRows, kk * 16), id_sq, kk > 0);
@@ -222,9 +228,9 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap q64, const __grid_con
         // dV += P^T dO
         if (!mbar_wait_bounded(p_ready, i & 1, abort_flag, a.spin_limit)) { ok = false; break; }
         tc_fence_after();
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < kBlk / 16; ++kk) {
-#pragma unroll
+#pragma unroll 1
           for (int c = 0; c < L::NCHUNK; ++c) {
             mma_ts(tmem + C::kDV + L::start(c), tmem + C::kST + kk * 8,
                    attn::mnmajor_desc<DP>(dot, kTileRows, c, kk * 16), idesc_f16(128, L::width(c), fmt, false, true),
@@ -234,9 +240,9 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap q64, const __grid_con
         // dK += dS^T Q, then dQ = dS K (dQ's TMEM columns must have been drained)
         if (!mbar_wait_bounded(ds_ready, i & 1, abort_flag, a.spin_limit)) { ok = false; break; }
         tc_fence_after();
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < kBlk / 16; ++kk) {
-#pragma unroll
+#pragma unroll 1
           for (int c = 0; c < L::NCHUNK; ++c) {
             mma_ts(tmem + C::kDK + L::start(c), tmem + C::kDPT + kk * 8,
                    attn::mnmajor_desc<DP>(qt, kTileRows, c, kk * 16), idesc_f16(128, L::width(c), fmt, false, true),
@@ -245,11 +251,11 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap q64, const __grid_con
         }
         if (i > 0 && !mbar_wait_bounded(dq_free, (i - 1) & 1, abort_flag, a.spin_limit)) { ok = false; break; }
         tc_fence_after();
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < kBlk / 16; ++kk) {
           // A = dS [128 queries x 16 keys], MN-major SW128: two 64-query atoms 16 KB apart
           const uint64_t ad = smem_desc(ds_addr + kk * 16 * 128, 16384, 1024, kSw128);
-#pragma unroll
+#pragma unroll 1
           for (int c = 0; c < L::NCHUNK; ++c) {
             mma_ss(tmem + C::kDQ + L::start(c), ad, attn::mnmajor_desc<DP>(k_addr, kTileRows, c, kk * 16),
                    idesc_f16(128, L::width(c), fmt, true, true), kk > 0 ? 1u : 0u);
@@ -265,7 +271,9 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap q64, const __grid_con
       for (uint32_t it = 0; it < a.spin_limit && !mbar_try_wait(drain, 0); ++it) {
       }
     }
-  } else if (warp < 6) {
+  }
+  } else if (warp < 8) {
+    regs_inc<kRegsWork>();
     // ------------------------------------------------------------ compute WG: one key per thread
     const int quarter = warp % 4;
     const int kr = quarter * 32 + lane;        // key row within the block (TMEM lane)
@@ -275,19 +283,20 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap q64, const __grid_con
     const uint32_t st_t = tmem + lane_addr + C::kST;
     const uint32_t dpt_t = tmem + lane_addr + C::kDPT;
     uint8_t* ds_smem = smem + C::kDSOff;
-    // one scan row per lane quarter: row w holds the diagonals of keys 32w .. 32w+31
-    float* scan = reinterpret_cast<float*>(smem + C::kScanOff) + quarter * 160;
-    volatile int* wg_fail = abort_flag + 1;   // written only before the first named barrier below
+    // Diagonal bins of this warp: bin 31 - lane + q collects dS[key, q]; within one red
+    // instruction the 32 lanes hit 32 different bins, and a bin's updates arrive in program
+    // order, so the sums are bitwise reproducible.
+    float* bins = reinterpret_cast<float*>(smem + C::kBinOff) + quarter * kBins;
+    const uint32_t bin_lane = smem_u32(bins + 31 - lane);
+    for (int j = lane; j < kBins; j += 32) bins[j] = 0.f;
+    __syncwarp();
     bool ok = true;
     for (int i = 0; i < nq; ++i) {
       const int s = i % NQS;
       const int q0 = i * kBlk;
       const bool w_ok = mbar_wait_bounded(sdp_ready, i & 1, abort_flag, a.spin_limit) &&
                         mbar_wait_bounded(&qdo_full[s], (i / NQS) & 1, abort_flag, a.spin_limit);
-      // All 128 threads take the same branch: warp-collective TMEM ops and named barriers follow.
-      if (!__all_sync(0xffffffffu, w_ok) && lane == 0) *wg_fail = 1;
-      named_bar(1, 128);
-      if (*wg_fail) {
+      if (!__all_sync(0xffffffffu, w_ok)) {   // warp-uniform: TMEM ops below are warp-collective
         ok = false;
         break;
       }
@@ -319,8 +328,8 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap q64, const __grid_con
       tc_fence_before();
       mbar_arrive(p_ready);
 
-      // dS^T = P^T (dP^T - delta), 32 queries at a time; diagonal scan along the way
-      float run = 0.f;
+      // dS^T = P^T (dP^T - delta), 32 queries at a time, into TMEM (dK MMA), smem (dQ MMA)
+      // and the diagonal bins (dBias)
 #pragma unroll
       for (int qc = 0; qc < kBlk / 32; ++qc) {
         uint32_t dpv[32];
@@ -333,15 +342,8 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap q64, const __grid_con
           const float ds0 = p[q] * (__uint_as_float(dpv[e]) - vec[128 + q]);
           const float ds1 = p[q + 1] * (__uint_as_float(dpv[e + 1]) - vec[128 + q + 1]);
           dk[e / 2] = F16 ? pack_f16x2(ds0, ds1) : pack_bf16x2(ds0, ds1);
-          // warp scan: after step q, lane 31 holds the sum of diagonal (31 - q) of this warp's keys
-          run = __shfl_up_sync(0xffffffffu, run, 1);
-          if (lane == 0) run = 0.f;
-          run += ds0;
-          if (lane == 31) scan[q] = run;
-          run = __shfl_up_sync(0xffffffffu, run, 1);
-          if (lane == 0) run = 0.f;
-          run += ds1;
-          if (lane == 31) scan[q + 1] = run;
+          red_add_shared(bin_lane + 4u * q, ds0);
+          red_add_shared(bin_lane + 4u * (q + 1), ds1);
         }
         tmem_st16(dpt_t + qc * 16, dk);
         // smem copy for the dQ MMA: row kr of 64-query atom (qc/2), 16-byte chunks (qc%2)*4..+3
@@ -353,34 +355,23 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap q64, const __grid_con
               make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
         }
       }
-#pragma unroll
-      for (int e = 0; e < 31; ++e) {   // flush: queries past the block contribute zero
-        run = __shfl_up_sync(0xffffffffu, run, 1);
-        if (lane == 0) run = 0.f;
-        if (lane == 31) scan[kBlk + e] = run;
-      }
       tmem_wait_st();
       fence_async_shared();   // dS smem writes -> visible to the MMA (async proxy)
       tc_fence_before();
       mbar_arrive(ds_ready);
-      // tile diagonal vector: T[e + 127] = sum over warps w of scan_w[31 - (e - 32 w)]
-      named_bar(1, 128);
-      float* out = a.dbias_part + (((size_t)bh * a.n_blk + kb) * a.n_blk + i) * kDiagPad;
-      const float* scan0 = reinterpret_cast<const float*>(smem + C::kScanOff);
-      for (int t = threadIdx.x - 64; t < kDiag; t += 128) {
-        const int e = t - (kBlk - 1);
-        float acc = 0.f;
+      // flush this warp's bins for the tile and clear them
+      __syncwarp();
+      float* out = a.dbias_part + ((((size_t)bh * a.n_blk + kb) * a.n_blk + i) * 4 + quarter) * kBins;
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          const int idx = 31 - (e - 32 * w);
-          if (idx >= 0 && idx < kScan) acc += scan0[w * 160 + idx];
-        }
-        out[t] = acc;
+      for (int j = lane; j < kBins; j += 32) {
+        out[j] = bins[j];
+        bins[j] = 0.f;
       }
-      named_bar(1, 128);   // scan buffer reusable
+      __syncwarp();
     }
     if (!ok) watchdog_fire(kWdBwdCompute);
   } else {
+    regs_inc<kRegsWork>();
     // ------------------------------------------------------------ dQ WG: one query row per thread
     const int quarter = warp % 4;
     const int r = quarter * 32 + lane;
@@ -512,25 +503,32 @@ relpos_bwd_dq_kernel(const float* __restrict__ dq_acc, void* __restrict__ dqkv, 
   *reinterpret_cast<uint4*>(reinterpret_cast<T*>(dqkv) + row * dqkv_stride + c) = pk;
 }
 
-// dpd[h, t] = sum over b, and over the tiles (kb, qb) whose diagonal range covers
-// g = t - (S-1) = key - query, of the tile vector entry g - 128 (kb - qb) + 127.  Fixed order.
+// dpd[h, t] = sum over b, over the tiles (kb, qb) whose diagonal range covers g = t - (S-1) =
+// key - query, and over the four key-quarter warps of each tile, of the bin holding g.  A tile at
+// offset d = kb - qb holds diagonal e = g - 128 d of quarter w in bin 31 - e + 32 w.  Fixed order:
+// deterministic.
 __global__ void __launch_bounds__(256)
 relpos_bwd_dpd_kernel(const float* __restrict__ part, float* __restrict__ dpd, int B, int S, int H, int nb) {
   const int h = blockIdx.y;
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= 2 * S - 1) return;
   const int g = t - (S - 1);
-  // tile offsets d = kb - qb with g - 128 d in [-127, 127]
   const int d_hi = (g + 127) >= 0 ? (g + 127) / 128 : -((-(g + 127) + 127) / 128);
   float acc = 0.f;
   for (int bb = 0; bb < B; ++bb) {
-    const float* pb = part + (size_t)(bb * H + h) * nb * nb * kDiagPad;
+    const float* pb = part + (size_t)(bb * H + h) * nb * nb * 4 * kBins;
     for (int d = d_hi; d >= d_hi - 1; --d) {
       const int e = g - 128 * d;
       if (e < -(kBlk - 1) || e > kBlk - 1) continue;
       const int kb_lo = d > 0 ? d : 0, kb_hi = d > 0 ? nb : nb + d;   // qb = kb - d in [0, nb)
-      for (int kbi = kb_lo; kbi < kb_hi; ++kbi)
-        acc += pb[((size_t)kbi * nb + (kbi - d)) * kDiagPad + e + (kBlk - 1)];
+      for (int kbi = kb_lo; kbi < kb_hi; ++kbi) {
+        const float* tile = pb + ((size_t)kbi * nb + (kbi - d)) * 4 * kBins;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          const int j = 31 - e + 32 * w;
+          if (j >= 0 && j < kBlk + 31) acc += tile[w * kBins + j];
+        }
+      }
     }
   }
   dpd[(size_t)h * (2 * S - 1) + t] = acc;
@@ -547,7 +545,7 @@ inline WsLayout ws_layout(int64_t B, int64_t S, int64_t H, int64_t D) {
   w.delta = 0;
   w.dq = up((size_t)B * H * S * 4);
   w.part = w.dq + up((size_t)B * S * H * D * 4);
-  w.total = w.part + up((size_t)B * H * nb * nb * kDiagPad * 4);
+  w.total = w.part + up((size_t)B * H * nb * nb * 4 * kBins * 4);
   return w;
 }
 

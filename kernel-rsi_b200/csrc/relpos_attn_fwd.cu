@@ -5,12 +5,13 @@
 //   m_i = max_j s2, l_i = sum_j exp2(s2 - m_i), out_i = sum_j exp2(s2 - m_i) v_j / l_i,
 //   lse_i = m_i + log2(l_i); out in the input dtype, out32 in fp32.
 //
-// Structure (one CTA = two 128-query tiles of one (b, h), 10 warps):
+// Structure (one CTA = two 128-query tiles of one (b, h), 12 warps = 3 warpgroups; setmaxnreg
+// moves registers from warpgroup 0 to the softmax warpgroups):
 //   warp 0      TMA producer: Q once; per 128-key block a K tile, a V tile (3-stage ring) and a
 //               slab of the 383 bias values that block needs (pre-multiplied by log2 e);
 //   warp 1      TMEM owner (512 columns) and the single-thread tcgen05.mma issuer:
 //               S_t = Q_t K^T (SS, K = DP) into TMEM, O_t += P_t V (TS: P read from TMEM);
-//   warps 2-5   softmax for query tile 0, warps 6-9 for tile 1 (one query row per thread,
+//   warps 4-7   softmax for query tile 0, warps 8-11 for tile 1 (one query row per thread,
 //               row = TMEM lane): S from TMEM -> bias add -> online softmax with the rescale of
 //               O skipped unless the running max grows by more than 2^8 -> P (bf16/f16) written
 //               back over S in TMEM -> at the end O / l to global memory.
@@ -35,7 +36,9 @@ using attn::kTileRows;
 
 constexpr int kBN = 128;            // keys per block
 constexpr int kQTiles = 2;          // query tiles per CTA
-constexpr int kThreads = 320;       // 10 warps
+constexpr int kThreads = 384;       // 3 warpgroups: {producer, MMA, -, -}, softmax tile 0, tile 1
+constexpr uint32_t kRegsCtl = 40;   // per-thread registers of warpgroup 0 after setmaxnreg
+constexpr uint32_t kRegsSm = 232;   // softmax warpgroups (launch: 168 x 384 = 128 x (56 + 2 x 224))
 constexpr int kSlab = 384;          // floats per bias slab (2*128 + 128 - 1 = 383 used)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;   // log2 units: P <= 2^8 between rescales
@@ -123,7 +126,10 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap m64, const __grid_constant
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
+  // Each role runs entirely inside the branch that sets its register budget, so ptxas compiles
+  // it against that budget.
+  if (warp < 4) {
+    regs_dec<kRegsCtl>();
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
@@ -164,9 +170,11 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap m64, const __grid_constant
       const uint32_t kv_addr = smem_u32(smem + C::kKVOff);
       bool ok = mbar_wait_bounded(q_full, 0, abort_flag, a.spin_limit) &&
                 mbar_wait_bounded(&kv_full[0], 0, abort_flag, a.spin_limit);
+      // Issue loops stay rolled: an MMA occupies the tensor pipe for hundreds of cycles, and
+      // unrolled descriptor arithmetic would be hoisted into registers this warp does not have.
       auto issue_qk = [&](int t, int j) {
         const uint32_t kt = kv_addr + (2 * (j % NS)) * C::kTile;
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < DP / 16; ++kk) {
           const uint64_t ad = attn::kmajor_desc<DP>(q_addr + t * C::kTile, kTileRows, kk * 16);
           const uint64_t bd = attn::kmajor_desc<DP>(kt, kTileRows, kk * 16);
@@ -175,7 +183,7 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap m64, const __grid_constant
       };
       auto issue_pv = [&](int t, int j) {
         const uint32_t vt = kv_addr + (2 * (j % NS) + 1) * C::kTile;
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < kBN / 16; ++kk) {
           const uint32_t a_tmem = tmem + C::kSCol + t * kBN + kk * 8;   // P: 2 x 16-bit per column
 #pragma unroll
@@ -222,9 +230,11 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap m64, const __grid_constant
       for (uint32_t i = 0; i < a.spin_limit && !mbar_try_wait(drain, 0); ++i) {
       }
     }
+  }
   } else {
-    // ------------------------------------------------------------ softmax (warps 2..9)
-    const int t = (warp - 2) / 4;                       // query tile
+    regs_inc<kRegsSm>();
+    // ------------------------------------------------------------ softmax (warps 4..11)
+    const int t = (warp - 4) / 4;                       // query tile
     const int quarter = warp % 4;                       // TMEM lane quarter of this warp
     const int r = quarter * 32 + lane;                  // row within the tile
     const int q = q0 + t * kTileRows + r;               // query index within the sequence
@@ -252,14 +262,19 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap m64, const __grid_constant
       }
       const float* slab = slabs + s * kSlab + slab_base;
       const int valid = a.S - j * kBN;                  // keys of this block inside the sequence
-      float mx = -INFINITY;
+      // 8 independent max chains (a single chain would serialise 128 dependent max ops)
+      float mxa[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mxa[k] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < kBN; ++c) {
         float v = fmaf(sv[c], a.scale_log2, slab[c]);
         v = c < valid ? v : -INFINITY;
         sv[c] = v;
-        mx = fmaxf(mx, v);
+        mxa[c % 8] = fmaxf(mxa[c % 8], v);
       }
+      const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
+                             fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
       const float m_new = fmaxf(m_run, mx);
       const bool need = m_new - m_run > kRescaleThreshold;   // true on the first block (m_run = -inf)
       float alpha = 1.f, m_use = m_run;
@@ -268,15 +283,18 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap m64, const __grid_constant
         m_use = m_new;
         alpha = ex2_approx(m_run - m_new);              // 0 on the first block
       }
-      float sum = 0.f;
+      float suma[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) suma[k] = 0.f;
       uint32_t pk[kBN / 2];
 #pragma unroll
       for (int c = 0; c < kBN; c += 2) {
         const float p0 = ex2_approx(sv[c] - m_use);
         const float p1 = ex2_approx(sv[c + 1] - m_use);
-        sum += p0 + p1;
+        suma[(c / 2) % 8] += p0 + p1;
         pk[c / 2] = F16 ? pack_f16x2(p0, p1) : pack_bf16x2(p0, p1);
       }
+      const float sum = ((suma[0] + suma[1]) + (suma[2] + suma[3])) + ((suma[4] + suma[5]) + (suma[6] + suma[7]));
       l_run = l_run * alpha + sum;
       m_run = m_use;
       tmem_st32(s_tmem, pk);
