@@ -40,13 +40,12 @@ int attn_padded_dim(int64_t D);   // relpos_attn_fwd.cu
 namespace {
 
 using namespace sm100;
-using attn::DLayout;
 using attn::kTileRows;
 
 constexpr int kBlk = 128;          // keys per CTA, queries per iteration
 constexpr int kThreads = 384;       // 3 warpgroups: {producer, MMA, -, -}, compute, dQ/epilogue
-constexpr uint32_t kRegsCtl = 56;   // after setmaxnreg (launch: 168 x 384 = 128 x (56 + 224 + 224))
-constexpr uint32_t kRegsWork = 224;
+constexpr uint32_t kRegsCtl = 96;   // after setmaxnreg (launch 168 x 384 >= 128 x (96 + 200 + 200))
+constexpr uint32_t kRegsWork = 200;
 constexpr int kBins = 160;          // per-warp diagonal bins: 32 keys x 128 queries -> 159 diagonals
 constexpr int kDiag = 2 * kBlk - 1;     // 255 diagonals per 128 x 128 tile
 
@@ -55,8 +54,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 template <int DP>
 struct BwdCfg {
-  using L = DLayout<DP>;
-  static constexpr uint32_t kTile = L::tile_bytes(kTileRows);
+  static constexpr uint32_t kTile = attn::Tile<DP>::kBytes;
   static constexpr int NQS = 2;                                   // Q/dO stages
   static constexpr uint32_t kKOff = 0;
   static constexpr uint32_t kVOff = kKOff + kTile;
@@ -98,12 +96,9 @@ __device__ __forceinline__ void red_add_shared(uint32_t smem_addr, float v) {
 
 template <int DP, bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
-relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap q64, const __grid_constant__ CUtensorMap q32,
-                       const __grid_constant__ CUtensorMap q16, const __grid_constant__ CUtensorMap o64,
-                       const __grid_constant__ CUtensorMap o32, const __grid_constant__ CUtensorMap o16,
+relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap omap,
                        const BwdArgs a) {
   using C = BwdCfg<DP>;
-  using L = DLayout<DP>;
   constexpr int NQS = C::NQS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -144,8 +139,8 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap q64, const __grid_con
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    prefetch_tensormap(&q64);
-    prefetch_tensormap(&o64);
+    prefetch_tensormap(&qmap);
+    prefetch_tensormap(&omap);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -163,8 +158,8 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap q64, const __grid_con
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       mbar_arrive_expect_tx(kv_full, 2 * C::kTile);
-      attn::load_tile<DP>(smem + C::kKOff, &q64, &q32, &q16, kv_full, a.H + h, k0, b);
-      attn::load_tile<DP>(smem + C::kVOff, &q64, &q32, &q16, kv_full, 2 * a.H + h, k0, b);
+      attn::load_tile<DP>(smem + C::kKOff, &qmap, kv_full, a.H + h, k0, b);
+      attn::load_tile<DP>(smem + C::kVOff, &qmap, kv_full, 2 * a.H + h, k0, b);
     }
     const int two_s = 2 * a.S - 1;
     const float* pdh = a.pd + (size_t)h * two_s;
@@ -180,8 +175,8 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap q64, const __grid_con
       uint8_t* qt = smem + C::kQOff + s * 2 * C::kTile;
       if (lane == 0) {
         mbar_arrive_expect_tx(&qdo_full[s], 2 * C::kTile);
-        attn::load_tile<DP>(qt, &q64, &q32, &q16, &qdo_full[s], h, q0, b);
-        attn::load_tile<DP>(qt + C::kTile, &o64, &o32, &o16, &qdo_full[s], h, q0, b);
+        attn::load_tile<DP>(qt, &qmap, &qdo_full[s], h, q0, b);
+        attn::load_tile<DP>(qt + C::kTile, &omap, &qdo_full[s], h, q0, b);
       }
       float* vec = reinterpret_cast<float*>(smem + C::kVecOff + s * C::kVecBytes);
       for (int r = lane; r < kBlk; r += 32) {
@@ -202,65 +197,53 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap q64, const __grid_con
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t fmt = F16 ? 0u : 1u;
-      constexpr uint32_t id_sq = idesc_f16(128, kBlk, fmt, false, false);   // S^T, dP^T
-      const uint32_t k_addr = smem_u32(smem + C::kKOff);
-      const uint32_t v_addr = smem_u32(smem + C::kVOff);
-      const uint32_t ds_addr = smem_u32(smem + C::kDSOff);
+      constexpr uint32_t id_sq = idesc_f16(128, kBlk, fmt, false, false);   // S^T, dP^T: K-major, N = 128
+      constexpr uint32_t id_nd = idesc_f16(128, DP, fmt, false, true);      // dV, dK: B MN-major, N = DP
+      constexpr uint32_t id_dq = idesc_f16(128, DP, fmt, true, true);       // dQ: A (dS) and B MN-major
+      // Precomputed descriptors (see relpos_attn_fwd.cu): issue = constant add + MMA.
+      const uint64_t k_kd = attn::kmajor_base(smem_u32(smem + C::kKOff));
+      const uint64_t v_kd = attn::kmajor_base(smem_u32(smem + C::kVOff));
+      const uint64_t k_mn = attn::mnmajor_base(smem_u32(smem + C::kKOff));
+      const uint64_t q_kd0 = attn::kmajor_base(smem_u32(smem + C::kQOff));
+      const uint64_t o_kd0 = attn::kmajor_base(smem_u32(smem + C::kQOff + C::kTile));
+      const uint64_t q_mn0 = attn::mnmajor_base(smem_u32(smem + C::kQOff));
+      const uint64_t o_mn0 = attn::mnmajor_base(smem_u32(smem + C::kQOff + C::kTile));
+      // dS: [128 queries x 128 keys] MN-major, 128B swizzle, two 64-query atoms 16 KB apart
+      const uint64_t ds_d = smem_desc(smem_u32(smem + C::kDSOff), 16384, 1024, kSw128);
+      constexpr uint64_t kStage = (2 * C::kTile) >> 4;
+      constexpr uint64_t kDsRows = (16 * 128) >> 4;   // next 16 keys of dS
       bool ok = mbar_wait_bounded(kv_full, 0, abort_flag, a.spin_limit);
       for (int i = 0; i < nq && ok; ++i) {
         const int s = i % NQS;
-        const uint32_t qt = smem_u32(smem + C::kQOff + s * 2 * C::kTile);
-        const uint32_t dot = qt + C::kTile;
+        const uint64_t so = (uint64_t)s * kStage;
         if (!mbar_wait_bounded(&qdo_full[s], (i / NQS) & 1, abort_flag, a.spin_limit)) { ok = false; break; }
         tc_fence_after();
         // S^T = K Q^T and dP^T = V dO^T (rows = keys)
-#pragma unroll 1
-        for (int kk = 0; kk < DP / 16; ++kk) {
-          mma_ss(tmem + C::kST, attn::kmajor_desc<DP>(k_addr, kTileRows, kk * 16),
-                 attn::kmajor_desc<DP>(qt, kTileRows, kk * 16), id_sq, kk > 0);
-        }
-#pragma unroll 1
-        for (int kk = 0; kk < DP / 16; ++kk) {
-          mma_ss(tmem + C::kDPT, attn::kmajor_desc<DP>(v_addr, kTileRows, kk * 16),
-                 attn::kmajor_desc<DP>(dot, kTileRows, kk * 16), id_sq, kk > 0);
-        }
+#pragma unroll
+        for (int kk = 0; kk < DP / 16; ++kk)
+          mma_ss(tmem + C::kST, k_kd + kk * attn::kKSliceStep, q_kd0 + so + kk * attn::kKSliceStep, id_sq, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < DP / 16; ++kk)
+          mma_ss(tmem + C::kDPT, v_kd + kk * attn::kKSliceStep, o_kd0 + so + kk * attn::kKSliceStep, id_sq, kk > 0);
         mma_commit(sdp_ready);
+        const uint32_t acc0 = i > 0 ? 1u : 0u;
         // dV += P^T dO
         if (!mbar_wait_bounded(p_ready, i & 1, abort_flag, a.spin_limit)) { ok = false; break; }
         tc_fence_after();
-#pragma unroll 1
-        for (int kk = 0; kk < kBlk / 16; ++kk) {
-#pragma unroll 1
-          for (int c = 0; c < L::NCHUNK; ++c) {
-            mma_ts(tmem + C::kDV + L::start(c), tmem + C::kST + kk * 8,
-                   attn::mnmajor_desc<DP>(dot, kTileRows, c, kk * 16), idesc_f16(128, L::width(c), fmt, false, true),
-                   (i > 0 || kk > 0) ? 1u : 0u);
-          }
-        }
+#pragma unroll
+        for (int kk = 0; kk < kBlk / 16; ++kk)
+          mma_ts(tmem + C::kDV, tmem + C::kST + kk * 8, o_mn0 + so + kk * attn::kKRowStep, id_nd, kk > 0 ? 1u : acc0);
         // dK += dS^T Q, then dQ = dS K (dQ's TMEM columns must have been drained)
         if (!mbar_wait_bounded(ds_ready, i & 1, abort_flag, a.spin_limit)) { ok = false; break; }
         tc_fence_after();
-#pragma unroll 1
-        for (int kk = 0; kk < kBlk / 16; ++kk) {
-#pragma unroll 1
-          for (int c = 0; c < L::NCHUNK; ++c) {
-            mma_ts(tmem + C::kDK + L::start(c), tmem + C::kDPT + kk * 8,
-                   attn::mnmajor_desc<DP>(qt, kTileRows, c, kk * 16), idesc_f16(128, L::width(c), fmt, false, true),
-                   (i > 0 || kk > 0) ? 1u : 0u);
-          }
-        }
+#pragma unroll
+        for (int kk = 0; kk < kBlk / 16; ++kk)
+          mma_ts(tmem + C::kDK, tmem + C::kDPT + kk * 8, q_mn0 + so + kk * attn::kKRowStep, id_nd, kk > 0 ? 1u : acc0);
         if (i > 0 && !mbar_wait_bounded(dq_free, (i - 1) & 1, abort_flag, a.spin_limit)) { ok = false; break; }
         tc_fence_after();
-#pragma unroll 1
-        for (int kk = 0; kk < kBlk / 16; ++kk) {
-          // A = dS [128 queries x 16 keys], MN-major SW128: two 64-query atoms 16 KB apart
-          const uint64_t ad = smem_desc(ds_addr + kk * 16 * 128, 16384, 1024, kSw128);
-#pragma unroll 1
-          for (int c = 0; c < L::NCHUNK; ++c) {
-            mma_ss(tmem + C::kDQ + L::start(c), ad, attn::mnmajor_desc<DP>(k_addr, kTileRows, c, kk * 16),
-                   idesc_f16(128, L::width(c), fmt, true, true), kk > 0 ? 1u : 0u);
-          }
-        }
+#pragma unroll
+        for (int kk = 0; kk < kBlk / 16; ++kk)
+          mma_ss(tmem + C::kDQ, ds_d + kk * kDsRows, k_mn + kk * attn::kKRowStep, id_dq, kk > 0 ? 1u : 0u);
         mma_commit(dq_ready);
         mma_commit(&qdo_empty[s]);
       }
@@ -550,7 +533,7 @@ inline WsLayout ws_layout(int64_t B, int64_t S, int64_t H, int64_t D) {
 }
 
 template <int DP, bool F16>
-int launch_bwd(const attn::HeadMaps& qm, const attn::HeadMaps& om, const BwdArgs& a, const void* dout,
+int launch_bwd(const CUtensorMap& qm, const CUtensorMap& om, const BwdArgs& a, const void* dout,
                const float* out32, float* dpd, cudaStream_t stream) {
   using C = BwdCfg<DP>;
   const int64_t tokens_heads = (int64_t)a.B * a.S * a.H;
@@ -559,7 +542,7 @@ int launch_bwd(const attn::HeadMaps& qm, const attn::HeadMaps& om, const BwdArgs
   KRSI_LAUNCH_CHECK();
   auto kern = relpos_bwd_main_kernel<DP, F16>;
   KRSI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem));
-  kern<<<dim3(a.n_blk, a.B * a.H), kThreads, C::kSmem, stream>>>(qm.m64, qm.m32, qm.m16, om.m64, om.m32, om.m16, a);
+  kern<<<dim3(a.n_blk, a.B * a.H), kThreads, C::kSmem, stream>>>(qm, om, a);
   KRSI_LAUNCH_CHECK();
   const int64_t rows = (int64_t)a.B * a.S;
   const int64_t items = rows * (a.H * a.D / 8);
@@ -573,7 +556,7 @@ int launch_bwd(const attn::HeadMaps& qm, const attn::HeadMaps& om, const BwdArgs
 }
 
 template <bool F16>
-int dispatch_dp(int DP, const attn::HeadMaps& qm, const attn::HeadMaps& om, const BwdArgs& a, const void* dout,
+int dispatch_dp(int DP, const CUtensorMap& qm, const CUtensorMap& om, const BwdArgs& a, const void* dout,
                 const float* out32, float* dpd, cudaStream_t s) {
   switch (DP) {
     case 32: return launch_bwd<32, F16>(qm, om, a, dout, out32, dpd, s);
@@ -617,10 +600,10 @@ extern "C" int krsi_relpos_attn_bwd(const void* dout, const void* qkv, int64_t q
   const WsLayout ws = ws_layout(B, S, H, D);
   if (!workspace || workspace_bytes < ws.total || !aligned16(workspace)) return KRSI_ERR_WORKSPACE;
   uint8_t* w = static_cast<uint8_t*>(workspace);
-  attn::HeadMaps qm, om;
+  CUtensorMap qm, om;
   const bool f16 = dtype == KRSI_F16;
-  if (!attn::make_head_maps(&qm, DP, qkv, qkv_row_stride, B, S, 3 * H, D, f16) ||
-      !attn::make_head_maps(&om, DP, dout, H * D, B, S, H, D, f16))
+  if (!attn::make_head_map(&qm, qkv, qkv_row_stride, B, S, 3 * H, D, f16) ||
+      !attn::make_head_map(&om, dout, H * D, B, S, H, D, f16))
     return KRSI_ERR_CUDA;
   BwdArgs a{pd,
             lse,

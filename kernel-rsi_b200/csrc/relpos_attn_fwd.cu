@@ -7,10 +7,12 @@
 //
 // Structure (one CTA = two 128-query tiles of one (b, h), 12 warps = 3 warpgroups; setmaxnreg
 // moves registers from warpgroup 0 to the softmax warpgroups):
-//   warp 0      TMA producer: Q once; per 128-key block a K tile, a V tile (3-stage ring) and a
+//   warp 0      TMA producer (tile layout: attn_common.cuh): Q once; per 128-key block a K tile,
+//               a V tile (3-stage ring) and a
 //               slab of the 383 bias values that block needs (pre-multiplied by log2 e);
 //   warp 1      TMEM owner (512 columns) and the single-thread tcgen05.mma issuer:
-//               S_t = Q_t K^T (SS, K = DP) into TMEM, O_t += P_t V (TS: P read from TMEM);
+//               S_t = Q_t K^T (SS, K = DP) into TMEM, O_t += P_t V (TS: P read from TMEM, one
+//               N = DP instruction per 16 keys);
 //   warps 4-7   softmax for query tile 0, warps 8-11 for tile 1 (one query row per thread,
 //               row = TMEM lane): S from TMEM -> bias add -> online softmax with the rescale of
 //               O skipped unless the running max grows by more than 2^8 -> P (bf16/f16) written
@@ -31,23 +33,21 @@ namespace krsi {
 namespace {
 
 using namespace sm100;
-using attn::DLayout;
 using attn::kTileRows;
 
 constexpr int kBN = 128;            // keys per block
 constexpr int kQTiles = 2;          // query tiles per CTA
 constexpr int kThreads = 384;       // 3 warpgroups: {producer, MMA, -, -}, softmax tile 0, tile 1
-constexpr uint32_t kRegsCtl = 40;   // per-thread registers of warpgroup 0 after setmaxnreg
-constexpr uint32_t kRegsSm = 232;   // softmax warpgroups (launch: 168 x 384 = 128 x (56 + 2 x 224))
+constexpr uint32_t kRegsCtl = 96;   // per-thread registers of warpgroup 0 after setmaxnreg
+constexpr uint32_t kRegsSm = 200;   // softmax warpgroups (launch 168 x 384 >= 128 x (96 + 2 x 200))
 constexpr int kSlab = 384;          // floats per bias slab (2*128 + 128 - 1 = 383 used)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;   // log2 units: P <= 2^8 between rescales
 
 template <int DP>
 struct FwdCfg {
-  using L = DLayout<DP>;
   static constexpr int NS = DP <= 96 ? 3 : 2;                      // K/V pipeline stages
-  static constexpr uint32_t kTile = L::tile_bytes(kTileRows);       // one 128 x DP tile
+  static constexpr uint32_t kTile = attn::Tile<DP>::kBytes;         // one 128 x DP tile
   static constexpr uint32_t kQOff = 0;
   static constexpr uint32_t kKVOff = kQOff + kQTiles * kTile;
   static constexpr uint32_t kSlabOff = kKVOff + NS * 2 * kTile;
@@ -74,10 +74,8 @@ struct FwdArgs {
 
 template <int DP, bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
-relpos_fwd_kernel(const __grid_constant__ CUtensorMap m64, const __grid_constant__ CUtensorMap m32,
-                  const __grid_constant__ CUtensorMap m16, const FwdArgs a) {
+relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
   using C = FwdCfg<DP>;
-  using L = DLayout<DP>;
   constexpr int NS = C::NS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -113,11 +111,7 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap m64, const __grid_constant
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 0 && lane == 0) {
-    prefetch_tensormap(&m64);
-    prefetch_tensormap(&m32);
-    prefetch_tensormap(&m16);
-  }
+  if (warp == 0 && lane == 0) prefetch_tensormap(&tmap);
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
@@ -135,7 +129,7 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap m64, const __grid_constant
     if (lane == 0) {
       mbar_arrive_expect_tx(q_full, kQTiles * C::kTile);
       for (int t = 0; t < kQTiles; ++t)
-        attn::load_tile<DP>(smem + C::kQOff + t * C::kTile, &m64, &m32, &m16, q_full, h, q0 + t * kTileRows, b);
+        attn::load_tile<DP>(smem + C::kQOff + t * C::kTile, &tmap, q_full, h, q0 + t * kTileRows, b);
     }
     const int two_s = 2 * a.S - 1;
     const float* pdh = a.pd + (size_t)h * two_s;
@@ -148,8 +142,8 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap m64, const __grid_constant
       uint8_t* kt = smem + C::kKVOff + (2 * s) * C::kTile;
       if (lane == 0) {
         mbar_arrive_expect_tx(&kv_full[s], 2 * C::kTile);
-        attn::load_tile<DP>(kt, &m64, &m32, &m16, &kv_full[s], a.H + h, j * kBN, b);
-        attn::load_tile<DP>(kt + C::kTile, &m64, &m32, &m16, &kv_full[s], 2 * a.H + h, j * kBN, b);
+        attn::load_tile<DP>(kt, &tmap, &kv_full[s], a.H + h, j * kBN, b);
+        attn::load_tile<DP>(kt + C::kTile, &tmap, &kv_full[s], 2 * a.H + h, j * kBN, b);
       }
       // bias slab: slab[idx] = pd[h, j*128 - q0 - 255 + idx + S - 1] * log2e, zero outside the table
       float* slab = slabs + s * kSlab;
@@ -165,34 +159,33 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap m64, const __grid_constant
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t fmt = F16 ? 0u : 1u;
-      constexpr uint32_t id_qk = idesc_f16(128, kBN, fmt, false, false);
-      const uint32_t q_addr = smem_u32(smem + C::kQOff);
-      const uint32_t kv_addr = smem_u32(smem + C::kKVOff);
+      constexpr uint32_t id_qk = idesc_f16(128, kBN, fmt, false, false);   // S = Q K^T: both K-major
+      constexpr uint32_t id_pv = idesc_f16(128, DP, fmt, false, true);     // O += P V: V MN-major, N = DP
+      // Descriptors are precomputed; an issue is a constant add and the MMA itself, which keeps
+      // one thread issuing at the tensor pipe's rate.
+      const uint64_t q_desc = attn::kmajor_base(smem_u32(smem + C::kQOff));
+      const uint64_t k_desc0 = attn::kmajor_base(smem_u32(smem + C::kKVOff));
+      const uint64_t v_desc0 = attn::mnmajor_base(smem_u32(smem + C::kKVOff + C::kTile));
+      constexpr uint64_t kStageStep = (2 * C::kTile) >> 4;
+      constexpr uint64_t kQTileStep = C::kTile >> 4;
       bool ok = mbar_wait_bounded(q_full, 0, abort_flag, a.spin_limit) &&
                 mbar_wait_bounded(&kv_full[0], 0, abort_flag, a.spin_limit);
-      // Issue loops stay rolled: an MMA occupies the tensor pipe for hundreds of cycles, and
-      // unrolled descriptor arithmetic would be hoisted into registers this warp does not have.
       auto issue_qk = [&](int t, int j) {
-        const uint32_t kt = kv_addr + (2 * (j % NS)) * C::kTile;
-#pragma unroll 1
-        for (int kk = 0; kk < DP / 16; ++kk) {
-          const uint64_t ad = attn::kmajor_desc<DP>(q_addr + t * C::kTile, kTileRows, kk * 16);
-          const uint64_t bd = attn::kmajor_desc<DP>(kt, kTileRows, kk * 16);
-          mma_ss(tmem + C::kSCol + t * kBN, ad, bd, id_qk, kk > 0 ? 1u : 0u);
-        }
+        const uint64_t qd = q_desc + (uint64_t)t * kQTileStep;
+        const uint64_t kd = k_desc0 + (uint64_t)(j % NS) * kStageStep;
+        const uint32_t d = tmem + C::kSCol + t * kBN;
+#pragma unroll
+        for (int kk = 0; kk < DP / 16; ++kk)
+          mma_ss(d, qd + kk * attn::kKSliceStep, kd + kk * attn::kKSliceStep, id_qk, kk > 0 ? 1u : 0u);
       };
       auto issue_pv = [&](int t, int j) {
-        const uint32_t vt = kv_addr + (2 * (j % NS) + 1) * C::kTile;
-#pragma unroll 1
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint32_t a_tmem = tmem + C::kSCol + t * kBN + kk * 8;   // P: 2 x 16-bit per column
+        const uint64_t vd = v_desc0 + (uint64_t)(j % NS) * kStageStep;
+        const uint32_t p_tmem = tmem + C::kSCol + t * kBN;   // P: 2 x 16-bit per column
+        const uint32_t d = tmem + C::kOCol + t * DP;
+        const uint32_t acc0 = j > 0 ? 1u : 0u;
 #pragma unroll
-          for (int c = 0; c < L::NCHUNK; ++c) {
-            const uint32_t id_pv = idesc_f16(128, L::width(c), fmt, false, true);
-            const uint64_t bd = attn::mnmajor_desc<DP>(vt, kTileRows, c, kk * 16);
-            mma_ts(tmem + C::kOCol + t * DP + L::start(c), a_tmem, bd, id_pv, (j > 0 || kk > 0) ? 1u : 0u);
-          }
-        }
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          mma_ts(d, p_tmem + kk * 8, vd + kk * attn::kKRowStep, id_pv, kk > 0 ? 1u : acc0);
       };
       if (ok) {
         tc_fence_after();
@@ -365,24 +358,24 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap m64, const __grid_constant
 }
 
 template <int DP, bool F16>
-int launch_fwd(const attn::HeadMaps& hm, const FwdArgs& a, cudaStream_t stream) {
+int launch_fwd(const CUtensorMap& tmap, const FwdArgs& a, cudaStream_t stream) {
   using C = FwdCfg<DP>;
   auto kern = relpos_fwd_kernel<DP, F16>;
   KRSI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem));
   dim3 grid((a.S + kQTiles * kTileRows - 1) / (kQTiles * kTileRows), a.B * a.H);
-  kern<<<grid, kThreads, C::kSmem, stream>>>(hm.m64, hm.m32, hm.m16, a);
+  kern<<<grid, kThreads, C::kSmem, stream>>>(tmap, a);
   KRSI_LAUNCH_CHECK();
   return KRSI_OK;
 }
 
 template <bool F16>
-int dispatch_dp(int DP, const attn::HeadMaps& hm, const FwdArgs& a, cudaStream_t s) {
+int dispatch_dp(int DP, const CUtensorMap& tmap, const FwdArgs& a, cudaStream_t s) {
   switch (DP) {
-    case 32: return launch_fwd<32, F16>(hm, a, s);
-    case 64: return launch_fwd<64, F16>(hm, a, s);
-    case 80: return launch_fwd<80, F16>(hm, a, s);
-    case 96: return launch_fwd<96, F16>(hm, a, s);
-    case 128: return launch_fwd<128, F16>(hm, a, s);
+    case 32: return launch_fwd<32, F16>(tmap, a, s);
+    case 64: return launch_fwd<64, F16>(tmap, a, s);
+    case 80: return launch_fwd<80, F16>(tmap, a, s);
+    case 96: return launch_fwd<96, F16>(tmap, a, s);
+    case 128: return launch_fwd<128, F16>(tmap, a, s);
     default: return KRSI_ERR_UNSUPPORTED;
   }
 }
@@ -417,10 +410,9 @@ extern "C" int krsi_relpos_attn_fwd(const void* qkv, int64_t qkv_row_stride, con
   if (qkv_row_stride % 8 != 0 || !aligned16(qkv) || !aligned16(out) || !aligned16(out32))
     return KRSI_ERR_MISALIGNED;
   if (S > (1 << 24) || B * H > 65535) return KRSI_ERR_UNSUPPORTED;
-  attn::HeadMaps hm;
-  if (!attn::make_head_maps(&hm, DP, qkv, qkv_row_stride, B, S, 3 * H, D, dtype == KRSI_F16))
-    return KRSI_ERR_CUDA;
+  CUtensorMap tmap;
+  if (!attn::make_head_map(&tmap, qkv, qkv_row_stride, B, S, 3 * H, D, dtype == KRSI_F16)) return KRSI_ERR_CUDA;
   FwdArgs a{pd, out, out32, lse, (int)B, (int)S, (int)H, (int)D, scale * 1.4426950408889634f,
             (int)((S + kBN - 1) / kBN), kSpinLimit};
-  return dtype == KRSI_F16 ? dispatch_dp<true>(DP, hm, a, stream) : dispatch_dp<false>(DP, hm, a, stream);
+  return dtype == KRSI_F16 ? dispatch_dp<true>(DP, tmap, a, stream) : dispatch_dp<false>(DP, tmap, a, stream);
 }
