@@ -64,9 +64,10 @@ struct BwdCfg {
   static constexpr uint32_t kVecBytes = (128 + 128 + 256) * 4;
   static constexpr uint32_t kBinOff = kVecOff + NQS * kVecBytes;  // 4 warps x kBins floats
   static constexpr uint32_t kBarOff = kBinOff + 4 * kBins * 4;
-  static constexpr int kNumBars = 1 + 2 * NQS + 7;
+  static constexpr int kNumBars = 1 + 2 * NQS + 8;
   static constexpr uint32_t kMiscOff = kBarOff + kNumBars * 8;
-  static constexpr uint32_t kSmem = kMiscOff + 16 + 1024;
+  static constexpr uint32_t kRowOff = kMiscOff + 16;   // resident pd / lse / delta rows (runtime length)
+  static constexpr uint32_t kSmem = kRowOff + 1024;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kST = 0, kDPT = 128, kDV = 256, kDK = 256 + DP, kDQ = 256 + 2 * DP;
   static_assert(kDQ + DP <= kTmemCols, "backward TMEM plan needs DP <= 80");
@@ -94,7 +95,15 @@ __device__ __forceinline__ void red_add_shared(uint32_t smem_addr, float v) {
   asm volatile("red.shared.add.f32 [%0], %1;" ::"r"(smem_addr), "f"(v) : "memory");
 }
 
-template <int DP, bool F16>
+// Resident rows (one load per CTA): pd[h, :] * log2(e) with kRowPad zeros before and 128 after
+// (every key - query + S - 1 a tile forms stays inside), then lse and delta of this (b, h), each
+// followed by 128 zeros for queries past S.
+constexpr int kRowPad = 256;
+__host__ __device__ constexpr int64_t pd_row_floats(int64_t S) { return 2 * S - 1 + kRowPad + 128; }
+__host__ __device__ constexpr int64_t vec_row_floats(int64_t S) { return S + 128; }
+__host__ __device__ constexpr int64_t rows_bytes(int64_t S) { return (pd_row_floats(S) + 2 * vec_row_floats(S)) * 4; }
+
+template <int DP, bool F16, bool RES>
 __global__ void __launch_bounds__(kThreads, 1)
 relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap omap,
                        const BwdArgs a) {
@@ -113,6 +122,10 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
   uint64_t* dq_free = sdp_ready + 4;
   uint64_t* kdv_done = sdp_ready + 5;
   uint64_t* drain = sdp_ready + 6;
+  uint64_t* row_full = sdp_ready + 7;
+  float* pd_row = reinterpret_cast<float*>(smem + C::kRowOff);
+  float* lse_row = pd_row + pd_row_floats(a.S);
+  float* del_row = lse_row + vec_row_floats(a.S);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
 
@@ -124,7 +137,7 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
     for (int s = 0; s < NQS; ++s) {
-      mbar_init(&qdo_full[s], 2);   // TMA expect_tx + vectors/slab stores
+      mbar_init(&qdo_full[s], RES ? 1 : 2);   // TMA expect_tx (+ vectors/slab stores)
       mbar_init(&qdo_empty[s], 1);
     }
     mbar_init(sdp_ready, 1);
@@ -134,6 +147,7 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
     mbar_init(dq_free, 128);
     mbar_init(kdv_done, 1);
     mbar_init(drain, 1);
+    mbar_init(row_full, 32);
     abort_flag[0] = 0;
     abort_flag[1] = 0;
     fence_barrier_init();
@@ -165,6 +179,36 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
     const float* pdh = a.pd + (size_t)h * two_s;
     const float* lse_bh = a.lse + (size_t)bh * a.S;
     const float* del_bh = a.delta + (size_t)bh * a.S;
+    if constexpr (RES) {
+      const int npd = (int)pd_row_floats(a.S), nv = (int)vec_row_floats(a.S);
+      for (int i0 = lane; i0 < npd; i0 += 32 * 4) {
+        float v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int pos = i0 + 32 * u - kRowPad;
+          v[u] = (pos >= 0 && pos < two_s) ? __ldg(pdh + pos) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (i0 + 32 * u < npd) pd_row[i0 + 32 * u] = v[u] * kLog2e;
+      }
+      for (int i0 = lane; i0 < nv; i0 += 32 * 2) {
+        float l4[2], d4[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int q = i0 + 32 * u;
+          l4[u] = q < a.S ? __ldg(lse_bh + q) : 0.f;
+          d4[u] = q < a.S ? __ldg(del_bh + q) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+          if (i0 + 32 * u < nv) {
+            lse_row[i0 + 32 * u] = l4[u];
+            del_row[i0 + 32 * u] = d4[u];
+          }
+      }
+      mbar_arrive(row_full);
+    }
     for (int i = 0; i < nq; ++i) {
       const int s = i % NQS;
       if (i >= NQS && !mbar_wait_bounded(&qdo_empty[s], ((i / NQS) + 1) & 1, abort_flag, a.spin_limit)) {
@@ -178,6 +222,7 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
         attn::load_tile<DP>(qt, &qmap, &qdo_full[s], h, q0, b);
         attn::load_tile<DP>(qt + C::kTile, &omap, &qdo_full[s], h, q0, b);
       }
+      if constexpr (RES) continue;
       float* vec = reinterpret_cast<float*>(smem + C::kVecOff + s * C::kVecBytes);
       for (int r = lane; r < kBlk; r += 32) {
         const int q = q0 + r;
@@ -273,19 +318,22 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
     const uint32_t bin_lane = smem_u32(bins + 31 - lane);
     for (int j = lane; j < kBins; j += 32) bins[j] = 0.f;
     __syncwarp();
-    bool ok = true;
-    for (int i = 0; i < nq; ++i) {
+    bool ok = !RES || __all_sync(0xffffffffu, mbar_wait_bounded(row_full, 0, abort_flag, a.spin_limit));
+    for (int i = 0; i < nq && ok; ++i) {
       const int s = i % NQS;
       const int q0 = i * kBlk;
       const bool w_ok = mbar_wait_bounded(sdp_ready, i & 1, abort_flag, a.spin_limit) &&
-                        mbar_wait_bounded(&qdo_full[s], (i / NQS) & 1, abort_flag, a.spin_limit);
+                        (RES || mbar_wait_bounded(&qdo_full[s], (i / NQS) & 1, abort_flag, a.spin_limit));
       if (!__all_sync(0xffffffffu, w_ok)) {   // warp-uniform: TMEM ops below are warp-collective
         ok = false;
         break;
       }
       tc_fence_after();
       const float* vec = reinterpret_cast<const float*>(smem + C::kVecOff + s * C::kVecBytes);
-      const float* slab = vec + 256 + kr + (kBlk - 1);   // slab[kr + 127 - q]
+      const float* lse_p = RES ? lse_row + q0 : vec;
+      const float* del_p = RES ? del_row + q0 : vec + 128;
+      // bias(key, q0 + q) = slab[-q]
+      const float* slab = RES ? pd_row + kRowPad + key - q0 + a.S - 1 : vec + 256 + kr + (kBlk - 1);
       const int qvalid = a.S - q0;
       float p[kBlk];
       {
@@ -301,7 +349,7 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const int q = qc * 32 + e;
-          const float s2 = fmaf(p[q], a.scale_log2, slab[-q]) - vec[q];
+          const float s2 = fmaf(p[q], a.scale_log2, slab[-q]) - lse_p[q];
           p[q] = (key_ok && q < qvalid) ? ex2_approx(s2) : 0.f;
           if (e & 1) pk[e / 2] = F16 ? pack_f16x2(p[q - 1], p[q]) : pack_bf16x2(p[q - 1], p[q]);
         }
@@ -322,8 +370,8 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
           const int q = qc * 32 + e;
-          const float ds0 = p[q] * (__uint_as_float(dpv[e]) - vec[128 + q]);
-          const float ds1 = p[q + 1] * (__uint_as_float(dpv[e + 1]) - vec[128 + q + 1]);
+          const float ds0 = p[q] * (__uint_as_float(dpv[e]) - del_p[q]);
+          const float ds1 = p[q + 1] * (__uint_as_float(dpv[e + 1]) - del_p[q + 1]);
           dk[e / 2] = F16 ? pack_f16x2(ds0, ds1) : pack_bf16x2(ds0, ds1);
           red_add_shared(bin_lane + 4u * q, ds0);
           red_add_shared(bin_lane + 4u * (q + 1), ds1);
@@ -540,9 +588,12 @@ int launch_bwd(const CUtensorMap& qm, const CUtensorMap& om, const BwdArgs& a, c
   relpos_bwd_prep_kernel<F16><<<(unsigned)((tokens_heads + 255) / 256), 256, 0, stream>>>(
       dout, out32, const_cast<float*>(a.delta), a.dq_acc, a.B, a.S, a.H, a.D);
   KRSI_LAUNCH_CHECK();
-  auto kern = relpos_bwd_main_kernel<DP, F16>;
-  KRSI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem));
-  kern<<<dim3(a.n_blk, a.B * a.H), kThreads, C::kSmem, stream>>>(qm, om, a);
+  const size_t res_smem = C::kSmem + (size_t)rows_bytes(a.S);
+  const bool res = res_smem <= 232448;   // 227 KB per CTA on sm_100
+  auto kern = res ? relpos_bwd_main_kernel<DP, F16, true> : relpos_bwd_main_kernel<DP, F16, false>;
+  const size_t smem = res ? res_smem : C::kSmem;
+  KRSI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  kern<<<dim3(a.n_blk, a.B * a.H), kThreads, smem, stream>>>(qm, om, a);
   KRSI_LAUNCH_CHECK();
   const int64_t rows = (int64_t)a.B * a.S;
   const int64_t items = rows * (a.H * a.D / 8);

@@ -52,9 +52,10 @@ struct FwdCfg {
   static constexpr uint32_t kKVOff = kQOff + kQTiles * kTile;
   static constexpr uint32_t kSlabOff = kKVOff + NS * 2 * kTile;
   static constexpr uint32_t kBarOff = kSlabOff + NS * kSlab * 4;
-  static constexpr int kNumBars = 1 + 2 * NS + 3 * kQTiles + 1;     // q_full, kv_full/empty, s/p/o, drain
+  static constexpr int kNumBars = 1 + 2 * NS + 3 * kQTiles + 2;     // q_full, kv_full/empty, s/p/o, drain, row
   static constexpr uint32_t kMiscOff = kBarOff + kNumBars * 8;
-  static constexpr uint32_t kSmem = kMiscOff + 16 + 1024;           // + alignment slack
+  static constexpr uint32_t kRowOff = kMiscOff + 16;                // resident bias row (runtime length)
+  static constexpr uint32_t kSmem = kRowOff + 1024;                 // static part + alignment slack
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kSCol = 0;                              // S_t at t*128
   static constexpr uint32_t kOCol = 256;                            // O_t at 256 + t*DP
@@ -72,7 +73,12 @@ struct FwdArgs {
   uint32_t spin_limit;
 };
 
-template <int DP, bool F16>
+// Resident bias row: pd[h, :] * log2(e) with kRowPad zeros before it and 128 after, so every
+// index a CTA forms (key - query + S - 1 for keys and queries up to 127 past S) stays inside.
+constexpr int kRowPad = 256;
+__host__ __device__ constexpr int64_t row_floats(int64_t S) { return 2 * S - 1 + kRowPad + 128; }
+
+template <int DP, bool F16, bool RES>
 __global__ void __launch_bounds__(kThreads, 1)
 relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
   using C = FwdCfg<DP>;
@@ -87,6 +93,8 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
   uint64_t* p_ready = s_ready + kQTiles;
   uint64_t* o_final = p_ready + kQTiles;
   uint64_t* drain = o_final + kQTiles;
+  uint64_t* row_full = drain + 1;
+  float* row = reinterpret_cast<float*>(smem + C::kRowOff);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
   float* slabs = reinterpret_cast<float*>(smem + C::kSlabOff);
@@ -99,7 +107,7 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < NS; ++s) {
-      mbar_init(&kv_full[s], 2);     // TMA expect_tx arrival + bias-slab arrival
+      mbar_init(&kv_full[s], RES ? 1 : 2);   // TMA expect_tx arrival (+ bias-slab arrival)
       mbar_init(&kv_empty[s], 1);    // tcgen05.commit
     }
     for (int t = 0; t < kQTiles; ++t) {
@@ -108,6 +116,7 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
       mbar_init(&o_final[t], 1);
     }
     mbar_init(drain, 1);
+    mbar_init(row_full, 32);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -133,6 +142,22 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
     }
     const int two_s = 2 * a.S - 1;
     const float* pdh = a.pd + (size_t)h * two_s;
+    if constexpr (RES) {
+      // pd row of head h, once per CTA; loads issued 8 at a time per lane
+      const int n = (int)row_floats(a.S);
+      for (int i0 = lane; i0 < n; i0 += 32 * 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int pos = i0 + 32 * u - kRowPad;
+          v[u] = (pos >= 0 && pos < two_s) ? __ldg(pdh + pos) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (i0 + 32 * u < n) row[i0 + 32 * u] = v[u] * kLog2e;
+      }
+      mbar_arrive(row_full);
+    }
     for (int j = 0; j < n_kb; ++j) {
       const int s = j % NS;
       if (j >= NS && !mbar_wait_bounded(&kv_empty[s], ((j / NS) + 1) & 1, abort_flag, a.spin_limit)) {
@@ -145,6 +170,7 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
         attn::load_tile<DP>(kt, &tmap, &kv_full[s], a.H + h, j * kBN, b);
         attn::load_tile<DP>(kt + C::kTile, &tmap, &kv_full[s], 2 * a.H + h, j * kBN, b);
       }
+      if constexpr (RES) continue;
       // bias slab: slab[idx] = pd[h, j*128 - q0 - 255 + idx + S - 1] * log2e, zero outside the table
       float* slab = slabs + s * kSlab;
       const int base = j * kBN - q0 - (kQTiles * kTileRows - 1) + a.S - 1;
@@ -235,12 +261,14 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
     const uint32_t s_tmem = tmem + lane_addr + C::kSCol + t * kBN;
     const uint32_t o_tmem = tmem + lane_addr + C::kOCol + t * DP;
     const int slab_base = (kQTiles - 1 - t) * kTileRows + (kTileRows - 1) - r;   // slab[slab_base + c]
+    // resident row: bias(q, key j*128 + c) = row[kRowPad + j*128 - q + S - 1 + c]
+    const float* row_q = row + kRowPad - q + a.S - 1;
     float m_run = -INFINITY, l_run = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n_kb; ++j) {
+    bool ok = !RES || __all_sync(0xffffffffu, mbar_wait_bounded(row_full, 0, abort_flag, a.spin_limit));
+    for (int j = 0; j < n_kb && ok; ++j) {
       const int s = j % NS;
       const bool w_ok = mbar_wait_bounded(&s_ready[t], j & 1, abort_flag, a.spin_limit) &&
-                        mbar_wait_bounded(&kv_full[s], (j / NS) & 1, abort_flag, a.spin_limit);
+                        (RES || mbar_wait_bounded(&kv_full[s], (j / NS) & 1, abort_flag, a.spin_limit));
       if (!__all_sync(0xffffffffu, w_ok)) {   // warp-uniform: TMEM loads/stores are warp-collective
         ok = false;
         break;
@@ -253,7 +281,7 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
         for (int c = 0; c < kBN; c += 32) tmem_ld32(s_tmem + c, u + c);
         tmem_wait_ld();
       }
-      const float* slab = slabs + s * kSlab + slab_base;
+      const float* slab = RES ? row_q + j * kBN : slabs + s * kSlab + slab_base;
       const int valid = a.S - j * kBN;                  // keys of this block inside the sequence
       // 8 independent max chains (a single chain would serialise 128 dependent max ops)
       float mxa[8];
@@ -357,13 +385,18 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
   if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
 }
 
+constexpr size_t kMaxSmem = 232448;   // 227 KB per CTA on sm_100
+
 template <int DP, bool F16>
 int launch_fwd(const CUtensorMap& tmap, const FwdArgs& a, cudaStream_t stream) {
   using C = FwdCfg<DP>;
-  auto kern = relpos_fwd_kernel<DP, F16>;
-  KRSI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem));
+  const size_t res_smem = C::kSmem + (size_t)row_floats(a.S) * 4;
+  const bool res = res_smem <= kMaxSmem;
+  auto kern = res ? relpos_fwd_kernel<DP, F16, true> : relpos_fwd_kernel<DP, F16, false>;
+  const size_t smem = res ? res_smem : C::kSmem;
+  KRSI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((a.S + kQTiles * kTileRows - 1) / (kQTiles * kTileRows), a.B * a.H);
-  kern<<<grid, kThreads, C::kSmem, stream>>>(tmap, a);
+  kern<<<grid, kThreads, smem, stream>>>(tmap, a);
   KRSI_LAUNCH_CHECK();
   return KRSI_OK;
 }
