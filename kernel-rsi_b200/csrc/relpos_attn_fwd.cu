@@ -7,16 +7,20 @@
 //
 // Structure (one CTA = two 128-query tiles of one (b, h), 12 warps = 3 warpgroups; setmaxnreg
 // moves registers from warpgroup 0 to the softmax warpgroups):
-//   warp 0      TMA producer (tile layout: attn_common.cuh): Q once; per 128-key block a K tile,
-//               a V tile (3-stage ring) and a
-//               slab of the 383 bias values that block needs (pre-multiplied by log2 e);
+//   warp 0      TMA producer (tile layout: attn_common.cuh): Q once, then per 128-key block a K
+//               tile and a V tile (3-stage ring);
+//   warps 2-3   the bias row pd[h, :] * log2(e), resident in shared memory for the CTA's life
+//               (two copies, one shifted by an element, for aligned pair reads), fetched with
+//               cp.async; sequences too long for it fall back to a per-block slab the producer
+//               writes;
 //   warp 1      TMEM owner (512 columns) and the single-thread tcgen05.mma issuer:
 //               S_t = Q_t K^T (SS, K = DP) into TMEM, O_t += P_t V (TS: P read from TMEM, one
 //               N = DP instruction per 16 keys);
 //   warps 4-7   softmax for query tile 0, warps 8-11 for tile 1 (one query row per thread,
-//               row = TMEM lane): S from TMEM -> bias add -> online softmax with the rescale of
-//               O skipped unless the running max grows by more than 2^8 -> P (bf16/f16) written
-//               back over S in TMEM -> at the end O / l to global memory.
+//               row = TMEM lane): S from TMEM -> bias add (paired fp32 FMAs) -> online softmax
+//               with the rescale of O skipped unless the running max grows by more than 2^8;
+//               exp2 on the SFU for 3/4 of the elements and on the FMA pipe (sm100.cuh) for
+//               1/4 -> P (bf16/f16) written back over S in TMEM -> at the end O / l to memory.
 // The two query tiles ping-pong so one tile's softmax overlaps the other tile's MMAs.
 // Every wait is bounded (watchdog.cuh); a stalled pipeline ends the CTA with an error word.
 #include <string.h>
@@ -75,8 +79,16 @@ struct FwdArgs {
 
 // Resident bias row: pd[h, :] * log2(e) with kRowPad zeros before it and 128 after, so every
 // index a CTA forms (key - query + S - 1 for keys and queries up to 127 past S) stays inside.
+// Two copies, the second shifted by one element, so that every thread reads its 128 bias values
+// as 8-byte aligned pairs (copy 0 when its start index is even, copy 1 when odd).
 constexpr int kRowPad = 256;
-__host__ __device__ constexpr int64_t row_floats(int64_t S) { return 2 * S - 1 + kRowPad + 128; }
+__host__ __device__ constexpr int64_t row_floats(int64_t S) { return (2 * S - 1 + kRowPad + 128 + 1) / 2 * 2; }
+__host__ __device__ constexpr int64_t row_bytes(int64_t S) { return 2 * row_floats(S) * 4; }
+
+__device__ __forceinline__ void cp_async4(float* smem_dst, const float* gsrc) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 template <int DP, bool F16, bool RES>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -94,7 +106,8 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
   uint64_t* o_final = p_ready + kQTiles;
   uint64_t* drain = o_final + kQTiles;
   uint64_t* row_full = drain + 1;
-  float* row = reinterpret_cast<float*>(smem + C::kRowOff);
+  float* row0 = reinterpret_cast<float*>(smem + C::kRowOff);
+  float* row1 = row0 + row_floats(a.S);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
   float* slabs = reinterpret_cast<float*>(smem + C::kSlabOff);
@@ -116,7 +129,7 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
       mbar_init(&o_final[t], 1);
     }
     mbar_init(drain, 1);
-    mbar_init(row_full, 32);
+    mbar_init(row_full, 64);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -142,22 +155,7 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
     }
     const int two_s = 2 * a.S - 1;
     const float* pdh = a.pd + (size_t)h * two_s;
-    if constexpr (RES) {
-      // pd row of head h, once per CTA; loads issued 8 at a time per lane
-      const int n = (int)row_floats(a.S);
-      for (int i0 = lane; i0 < n; i0 += 32 * 8) {
-        float v[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int pos = i0 + 32 * u - kRowPad;
-          v[u] = (pos >= 0 && pos < two_s) ? __ldg(pdh + pos) : 0.f;
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-          if (i0 + 32 * u < n) row[i0 + 32 * u] = v[u] * kLog2e;
-      }
-      mbar_arrive(row_full);
-    }
+
     for (int j = 0; j < n_kb; ++j) {
       const int s = j % NS;
       if (j >= NS && !mbar_wait_bounded(&kv_empty[s], ((j / NS) + 1) & 1, abort_flag, a.spin_limit)) {
@@ -180,6 +178,27 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&kv_full[s]);
+    }
+  } else if (warp == 2 || warp == 3) {
+    // ------------------------------------------------------------ resident bias rows (RES)
+    // cp.async keeps every load of the row in flight at once; each thread then scales its own
+    // elements by log2(e) (its copies have landed after wait_all) and arrives.
+    if constexpr (RES) {
+      const int two_s = 2 * a.S - 1;
+      const float* pdh = a.pd + (size_t)h * two_s;
+      const int n = (int)row_floats(a.S);
+      const int tid = threadIdx.x - 64;
+      for (int i = tid; i < n; i += 64) {
+        const int pos = i - kRowPad;
+        if (pos >= 0 && pos < two_s) cp_async4(row0 + i, pdh + pos); else row0[i] = 0.f;
+        if (pos + 1 >= 0 && pos + 1 < two_s) cp_async4(row1 + i, pdh + pos + 1); else row1[i] = 0.f;
+      }
+      cp_async_wait_all();
+      for (int i = tid; i < n; i += 64) {
+        row0[i] *= kLog2e;
+        row1[i] *= kLog2e;
+      }
+      mbar_arrive(row_full);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -261,8 +280,10 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
     const uint32_t s_tmem = tmem + lane_addr + C::kSCol + t * kBN;
     const uint32_t o_tmem = tmem + lane_addr + C::kOCol + t * DP;
     const int slab_base = (kQTiles - 1 - t) * kTileRows + (kTileRows - 1) - r;   // slab[slab_base + c]
-    // resident row: bias(q, key j*128 + c) = row[kRowPad + j*128 - q + S - 1 + c]
-    const float* row_q = row + kRowPad - q + a.S - 1;
+    // resident row: bias(q, key j*128 + c) = row0[bidx + c], bidx = kRowPad + j*128 - q + S - 1
+    const int bidx0 = kRowPad - q + a.S - 1;
+    const float* bias_q = (bidx0 & 1) ? row1 + bidx0 - 1 : row0 + bidx0;   // 8-byte aligned pairs
+    const uint64_t scale2 = f2_pack(a.scale_log2, a.scale_log2);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = !RES || __all_sync(0xffffffffu, mbar_wait_bounded(row_full, 0, abort_flag, a.spin_limit));
     for (int j = 0; j < n_kb && ok; ++j) {
@@ -274,28 +295,42 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
         break;
       }
       tc_fence_after();
-      float sv[kBN];
-      {
-        uint32_t* u = reinterpret_cast<uint32_t*>(sv);
+      uint32_t u[kBN];
 #pragma unroll
-        for (int c = 0; c < kBN; c += 32) tmem_ld32(s_tmem + c, u + c);
-        tmem_wait_ld();
+      for (int c = 0; c < kBN; c += 32) tmem_ld32(s_tmem + c, u + c);
+      tmem_wait_ld();
+      // v = s * scale * log2(e) + bias * log2(e), two columns per instruction
+      uint64_t v2[kBN / 2];
+      if constexpr (RES) {
+        const uint64_t* bp = reinterpret_cast<const uint64_t*>(bias_q + j * kBN);
+#pragma unroll
+        for (int i = 0; i < kBN / 2; ++i)
+          v2[i] = f2_fma(f2_pack(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1])), scale2, bp[i]);
+      } else {
+        const float* slab = slabs + s * kSlab + slab_base;
+#pragma unroll
+        for (int i = 0; i < kBN / 2; ++i)
+          v2[i] = f2_fma(f2_pack(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1])), scale2,
+                         f2_pack(slab[2 * i], slab[2 * i + 1]));
       }
-      const float* slab = RES ? row_q + j * kBN : slabs + s * kSlab + slab_base;
       const int valid = a.S - j * kBN;                  // keys of this block inside the sequence
-      // 8 independent max chains (a single chain would serialise 128 dependent max ops)
-      float mxa[8];
+      if (valid < kBN) {                                // only the last block of a ragged sequence
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mxa[k] = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < kBN; ++c) {
-        float v = fmaf(sv[c], a.scale_log2, slab[c]);
-        v = c < valid ? v : -INFINITY;
-        sv[c] = v;
-        mxa[c % 8] = fmaxf(mxa[c % 8], v);
+        for (int i = 0; i < kBN / 2; ++i) {
+          float lo, hi;
+          f2_unpack(v2[i], lo, hi);
+          v2[i] = f2_pack(2 * i < valid ? lo : -INFINITY, 2 * i + 1 < valid ? hi : -INFINITY);
+        }
       }
-      const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
-                             fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
+      // row max: 3-input max, 4 independent chains
+      float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int i = 0; i < kBN / 2; ++i) {
+        float lo, hi;
+        f2_unpack(v2[i], lo, hi);
+        mxa[i % 4] = max3(mxa[i % 4], lo, hi);
+      }
+      const float mx = fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3]));
       const float m_new = fmaxf(m_run, mx);
       const bool need = m_new - m_run > kRescaleThreshold;   // true on the first block (m_run = -inf)
       float alpha = 1.f, m_use = m_run;
@@ -304,18 +339,27 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
         m_use = m_new;
         alpha = ex2_approx(m_run - m_new);              // 0 on the first block
       }
-      float suma[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) suma[k] = 0.f;
+      // p = 2^(v - m): three of every four pairs on the SFU, one on the FMA pipe (balances the
+      // SFU against the issue slots); row sum in 4 paired chains; P packed to 16-bit pairs
+      const uint64_t negm2 = f2_pack(-m_use, -m_use);
+      uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
       uint32_t pk[kBN / 2];
 #pragma unroll
-      for (int c = 0; c < kBN; c += 2) {
-        const float p0 = ex2_approx(sv[c] - m_use);
-        const float p1 = ex2_approx(sv[c + 1] - m_use);
-        suma[(c / 2) % 8] += p0 + p1;
-        pk[c / 2] = F16 ? pack_f16x2(p0, p1) : pack_bf16x2(p0, p1);
+      for (int i = 0; i < kBN / 2; ++i) {
+        float x0, x1, p0, p1;
+        f2_unpack(f2_add(v2[i], negm2), x0, x1);
+        if (i % 4 == 3) {
+          exp2_poly3_x2(x0, x1, p0, p1);
+        } else {
+          p0 = ex2_approx(x0);
+          p1 = ex2_approx(x1);
+        }
+        acc2[i % 4] = f2_add(acc2[i % 4], f2_pack(p0, p1));
+        pk[i] = F16 ? pack_f16x2(p0, p1) : pack_bf16x2(p0, p1);
       }
-      const float sum = ((suma[0] + suma[1]) + (suma[2] + suma[3])) + ((suma[4] + suma[5]) + (suma[6] + suma[7]));
+      float sum_lo, sum_hi;
+      f2_unpack(f2_add(f2_add(acc2[0], acc2[1]), f2_add(acc2[2], acc2[3])), sum_lo, sum_hi);
+      const float sum = sum_lo + sum_hi;
       l_run = l_run * alpha + sum;
       m_run = m_use;
       tmem_st32(s_tmem, pk);
@@ -390,7 +434,7 @@ constexpr size_t kMaxSmem = 232448;   // 227 KB per CTA on sm_100
 template <int DP, bool F16>
 int launch_fwd(const CUtensorMap& tmap, const FwdArgs& a, cudaStream_t stream) {
   using C = FwdCfg<DP>;
-  const size_t res_smem = C::kSmem + (size_t)row_floats(a.S) * 4;
+  const size_t res_smem = C::kSmem + (size_t)row_bytes(a.S);
   const bool res = res_smem <= kMaxSmem;
   auto kern = res ? relpos_fwd_kernel<DP, F16, true> : relpos_fwd_kernel<DP, F16, false>;
   const size_t smem = res ? res_smem : C::kSmem;

@@ -212,3 +212,62 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
 
 }  // namespace sm100
 }  // namespace krsi
+
+// ---------------------------------------------------------------- packed fp32 and exp2
+namespace krsi {
+namespace sm100 {
+
+// Two fp32 lanes in one 64-bit register: Blackwell's paired FMA-pipe instructions.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x on the FMA pipe, for x <= 128: Cody-Waite style range reduction x = n + f with
+// n = round(x) (adding 1.5 * 2^23 rounds to an integer held in the low mantissa bits) and
+// f in [-1/2, 1/2], then 2^f from a degree-3 polynomial whose coefficients were fitted here for
+// minimum relative error on [-1/2, 1/2] (max relative error 7.5e-5 in fp32, below bf16's 2^-9
+// rounding of P), and 2^n added to the exponent field.  x is clamped at -125 (the smallest n for
+// which exponent(2^f) + n stays a normal exponent), so masked entries (-inf) give about 2^-125:
+// zero for every later use.  Valid for x <= 128.  Two lanes per call.
+__device__ __forceinline__ void exp2_poly3_x2(float x0, float x1, float& y0, float& y1) {
+  constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
+  x0 = fmaxf(x0, -125.0f);
+  x1 = fmaxf(x1, -125.0f);
+  const uint64_t x = f2_pack(x0, x1);
+  const uint64_t j = f2_add(x, f2_pack(kMagic, kMagic));            // round(x) + magic
+  const uint64_t r = f2_add(j, f2_pack(-kMagic, -kMagic));          // round(x)
+  const uint64_t f = f2_add(x, r ^ 0x8000000080000000ull);         // x - round(x)
+  uint64_t p = f2_fma(f2_pack(0.05517162382602692f, 0.05517162382602692f), f,
+                      f2_pack(0.2426111251115799f, 0.2426111251115799f));
+  p = f2_fma(p, f, f2_pack(0.6932609677314758f, 0.6932609677314758f));
+  p = f2_fma(p, f, f2_pack(0.9999280571937561f, 0.9999280571937561f));
+  float p0, p1, j0, j1;
+  f2_unpack(p, p0, p1);
+  f2_unpack(j, j0, j1);
+  // the low mantissa bits of j hold round(x) (two's complement); (bits(magic) << 23) wraps to 0
+  y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(j0) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(j1) << 23));
+}
+
+}  // namespace sm100
+}  // namespace krsi
