@@ -56,6 +56,40 @@ __device__ __forceinline__ void load_tile(uint8_t* smem_tile, const CUtensorMap*
     sm100::tma_load_4d(smem_tile + c * kBlockBytes, map, bar, 16 * c, head_coord, row0, b);
 }
 
+// Fills dst[i] = src[i - pad] * mul for i in [0, n), zero where i - pad is outside [0, len).  Run by
+// `nthr` cooperating threads (tid in [0, nthr)); the 16-byte-aligned interior of src is read with
+// 128-bit loads, four in flight per thread, so a row of a few thousand floats takes one or two
+// memory round trips.  dst may have any 4-byte alignment.
+__device__ __forceinline__ void fill_row(float* dst, int n, int pad, const float* __restrict__ src, int len, float mul,
+                                         int tid, int nthr) {
+  const int mis = (int)((reinterpret_cast<uintptr_t>(src) >> 2) & 3);
+  const int a0 = mis ? min(4 - mis, len) : 0;         // first 16-byte aligned source index
+  const int nvec = len > a0 ? (len - a0) / 4 : 0;
+  const int a1 = a0 + 4 * nvec;                        // end of the vector interior
+  const float4* src4 = reinterpret_cast<const float4*>(src + a0);
+  for (int v0 = tid; v0 < nvec; v0 += 4 * nthr) {
+    float4 x[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (v0 + u * nthr < nvec) x[u] = __ldg(src4 + v0 + u * nthr);
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (v0 + u * nthr < nvec) {
+        float* d = dst + pad + a0 + 4 * (v0 + u * nthr);
+        d[0] = x[u].x * mul;
+        d[1] = x[u].y * mul;
+        d[2] = x[u].z * mul;
+        d[3] = x[u].w * mul;
+      }
+  }
+  // source edges and the zero pads
+  for (int i = tid; i < n; i += nthr) {
+    const int p = i - pad;
+    if (p < 0 || p >= len) dst[i] = 0.f;
+    else if (p < a0 || p >= a1) dst[i] = __ldg(src + p) * mul;
+  }
+}
+
 // ---------------------------------------------------------------- host side
 using EncodeTiledFn = PFN_cuTensorMapEncodeTiled_v12000;
 

@@ -44,8 +44,9 @@ using attn::kTileRows;
 
 constexpr int kBlk = 128;          // keys per CTA, queries per iteration
 constexpr int kThreads = 384;       // 3 warpgroups: {producer, MMA, -, -}, compute, dQ/epilogue
-constexpr uint32_t kRegsCtl = 96;   // after setmaxnreg (launch 168 x 384 >= 128 x (96 + 200 + 200))
-constexpr uint32_t kRegsWork = 200;
+constexpr uint32_t kRegsCtl = 96;   // after setmaxnreg (launch 168 x 384 = 128 x (96 + 248 + 160))
+constexpr uint32_t kRegsCompute = 248;
+constexpr uint32_t kRegsDq = 160;
 constexpr int kBins = 160;          // per-warp diagonal bins: 32 keys x 128 queries -> 159 diagonals
 constexpr int kDiag = 2 * kBlk - 1;     // 255 diagonals per 128 x 128 tile
 
@@ -62,8 +63,7 @@ struct BwdCfg {
   static constexpr uint32_t kDSOff = kQOff + NQS * 2 * kTile;     // dS (bf16, MN-major SW128): 2 x 16 KB
   static constexpr uint32_t kVecOff = kDSOff + 2 * 16384;         // per stage: lse[128], delta[128], slab[256]
   static constexpr uint32_t kVecBytes = (128 + 128 + 256) * 4;
-  static constexpr uint32_t kBinOff = kVecOff + NQS * kVecBytes;  // 4 warps x kBins floats
-  static constexpr uint32_t kBarOff = kBinOff + 4 * kBins * 4;
+  static constexpr uint32_t kBarOff = kVecOff + NQS * kVecBytes;
   static constexpr int kNumBars = 1 + 2 * NQS + 8;
   static constexpr uint32_t kMiscOff = kBarOff + kNumBars * 8;
   static constexpr uint32_t kRowOff = kMiscOff + 16;   // resident pd / lse / delta rows (runtime length)
@@ -91,9 +91,6 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
                : "memory");
 }
 
-__device__ __forceinline__ void red_add_shared(uint32_t smem_addr, float v) {
-  asm volatile("red.shared.add.f32 [%0], %1;" ::"r"(smem_addr), "f"(v) : "memory");
-}
 
 // Resident rows (one load per CTA): pd[h, :] * log2(e) with kRowPad zeros before and 128 after
 // (every key - query + S - 1 a tile forms stays inside), then lse and delta of this (b, h), each
@@ -147,7 +144,7 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
     mbar_init(dq_free, 128);
     mbar_init(kdv_done, 1);
     mbar_init(drain, 1);
-    mbar_init(row_full, 32);
+    mbar_init(row_full, 64);
     abort_flag[0] = 0;
     abort_flag[1] = 0;
     fence_barrier_init();
@@ -179,36 +176,7 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
     const float* pdh = a.pd + (size_t)h * two_s;
     const float* lse_bh = a.lse + (size_t)bh * a.S;
     const float* del_bh = a.delta + (size_t)bh * a.S;
-    if constexpr (RES) {
-      const int npd = (int)pd_row_floats(a.S), nv = (int)vec_row_floats(a.S);
-      for (int i0 = lane; i0 < npd; i0 += 32 * 4) {
-        float v[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int pos = i0 + 32 * u - kRowPad;
-          v[u] = (pos >= 0 && pos < two_s) ? __ldg(pdh + pos) : 0.f;
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (i0 + 32 * u < npd) pd_row[i0 + 32 * u] = v[u] * kLog2e;
-      }
-      for (int i0 = lane; i0 < nv; i0 += 32 * 2) {
-        float l4[2], d4[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int q = i0 + 32 * u;
-          l4[u] = q < a.S ? __ldg(lse_bh + q) : 0.f;
-          d4[u] = q < a.S ? __ldg(del_bh + q) : 0.f;
-        }
-#pragma unroll
-        for (int u = 0; u < 2; ++u)
-          if (i0 + 32 * u < nv) {
-            lse_row[i0 + 32 * u] = l4[u];
-            del_row[i0 + 32 * u] = d4[u];
-          }
-      }
-      mbar_arrive(row_full);
-    }
+
     for (int i = 0; i < nq; ++i) {
       const int s = i % NQS;
       if (i >= NQS && !mbar_wait_bounded(&qdo_empty[s], ((i / NQS) + 1) & 1, abort_flag, a.spin_limit)) {
@@ -237,6 +205,16 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&qdo_full[s]);
+    }
+  } else if (warp == 2 || warp == 3) {
+    // ------------------------------------------------------------ resident rows (RES)
+    if constexpr (RES) {
+      const int tid = threadIdx.x - 64;
+      const int two_s = 2 * a.S - 1;
+      attn::fill_row(pd_row, (int)pd_row_floats(a.S), kRowPad, a.pd + (size_t)h * two_s, two_s, kLog2e, tid, 64);
+      attn::fill_row(lse_row, (int)vec_row_floats(a.S), 0, a.lse + (size_t)bh * a.S, a.S, 1.f, tid, 64);
+      attn::fill_row(del_row, (int)vec_row_floats(a.S), 0, a.delta + (size_t)bh * a.S, a.S, 1.f, tid, 64);
+      mbar_arrive(row_full);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -301,7 +279,7 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
     }
   }
   } else if (warp < 8) {
-    regs_inc<kRegsWork>();
+    regs_inc<kRegsCompute>();
     // ------------------------------------------------------------ compute WG: one key per thread
     const int quarter = warp % 4;
     const int kr = quarter * 32 + lane;        // key row within the block (TMEM lane)
@@ -311,13 +289,11 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
     const uint32_t st_t = tmem + lane_addr + C::kST;
     const uint32_t dpt_t = tmem + lane_addr + C::kDPT;
     uint8_t* ds_smem = smem + C::kDSOff;
-    // Diagonal bins of this warp: bin 31 - lane + q collects dS[key, q]; within one red
-    // instruction the 32 lanes hit 32 different bins, and a bin's updates arrive in program
-    // order, so the sums are bitwise reproducible.
-    float* bins = reinterpret_cast<float*>(smem + C::kBinOff) + quarter * kBins;
-    const uint32_t bin_lane = smem_u32(bins + 31 - lane);
-    for (int j = lane; j < kBins; j += 32) bins[j] = 0.f;
-    __syncwarp();
+    // dBias: this warp's 32 keys x 128 queries of dS touch 159 diagonals ("bins"): bin j holds
+    // key - query = 32 * quarter + 31 - j within the tile.  Each 32 x 32 sub-tile is transposed
+    // along its diagonals by 32 independent shuffles (lane l reads dS[(l + m) & 31][m]), so lane l
+    // owns bins 31 - l + 32 k (k = 0..4) and sums them in registers in a fixed order:
+    // deterministic, no atomics, no serial chain.
     bool ok = !RES || __all_sync(0xffffffffu, mbar_wait_bounded(row_full, 0, abort_flag, a.spin_limit));
     for (int i = 0; i < nq && ok; ++i) {
       const int s = i % NQS;
@@ -360,22 +336,23 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
       mbar_arrive(p_ready);
 
       // dS^T = P^T (dP^T - delta), 32 queries at a time, into TMEM (dK MMA), smem (dQ MMA)
-      // and the diagonal bins (dBias)
+      // and the diagonal registers (dBias)
+      float dbin[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int qc = 0; qc < kBlk / 32; ++qc) {
-        uint32_t dpv[32];
-        tmem_ld32(dpt_t + qc * 32, dpv);
+        uint32_t dsv[32];
+        tmem_ld32(dpt_t + qc * 32, dsv);
         tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int q = qc * 32 + e;
+          dsv[e] = __float_as_uint(p[q] * (__uint_as_float(dsv[e]) - del_p[q]));
+        }
         uint32_t dk[16];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const int q = qc * 32 + e;
-          const float ds0 = p[q] * (__uint_as_float(dpv[e]) - del_p[q]);
-          const float ds1 = p[q + 1] * (__uint_as_float(dpv[e + 1]) - del_p[q + 1]);
-          dk[e / 2] = F16 ? pack_f16x2(ds0, ds1) : pack_bf16x2(ds0, ds1);
-          red_add_shared(bin_lane + 4u * q, ds0);
-          red_add_shared(bin_lane + 4u * (q + 1), ds1);
-        }
+        for (int e = 0; e < 16; ++e)
+          dk[e] = F16 ? pack_f16x2(__uint_as_float(dsv[2 * e]), __uint_as_float(dsv[2 * e + 1]))
+                      : pack_bf16x2(__uint_as_float(dsv[2 * e]), __uint_as_float(dsv[2 * e + 1]));
         tmem_st16(dpt_t + qc * 16, dk);
         // smem copy for the dQ MMA: row kr of 64-query atom (qc/2), 16-byte chunks (qc%2)*4..+3
         uint8_t* row = ds_smem + (qc / 2) * 16384 + kr * 128;
@@ -385,24 +362,32 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
           *reinterpret_cast<uint4*>(row + ((chunk ^ (kr & 7)) << 4)) =
               make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
         }
+        // diagonal transpose of this 32 x 32 sub-tile: m < 32 - lane stays on diagonal +lane
+        float hi = 0.f, lo = 0.f;
+#pragma unroll
+        for (int m = 0; m < 32; ++m) {
+          const float x = __shfl_sync(0xffffffffu, __uint_as_float(dsv[m]), (lane + m) & 31);
+          if (m < 32 - lane) hi += x;
+          else lo += x;
+        }
+        dbin[qc] += hi;
+        dbin[qc + 1] += lo;
       }
       tmem_wait_st();
       fence_async_shared();   // dS smem writes -> visible to the MMA (async proxy)
       tc_fence_before();
       mbar_arrive(ds_ready);
-      // flush this warp's bins for the tile and clear them
-      __syncwarp();
+      // this tile's diagonal sums: lane owns bins 31 - lane + 32 k
       float* out = a.dbias_part + ((((size_t)bh * a.n_blk + kb) * a.n_blk + i) * 4 + quarter) * kBins;
 #pragma unroll
-      for (int j = lane; j < kBins; j += 32) {
-        out[j] = bins[j];
-        bins[j] = 0.f;
+      for (int k = 0; k < 5; ++k) {
+        const int bin = 31 - lane + 32 * k;
+        if (bin < kBins) out[bin] = dbin[k];
       }
-      __syncwarp();
     }
     if (!ok) watchdog_fire(kWdBwdCompute);
   } else {
-    regs_inc<kRegsWork>();
+    regs_dec<kRegsDq>();
     // ------------------------------------------------------------ dQ WG: one query row per thread
     const int quarter = warp % 4;
     const int r = quarter * 32 + lane;

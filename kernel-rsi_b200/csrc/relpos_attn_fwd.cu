@@ -11,8 +11,8 @@
 //               tile and a V tile (3-stage ring);
 //   warps 2-3   the bias row pd[h, :] * log2(e), resident in shared memory for the CTA's life
 //               (two copies, one shifted by an element, for aligned pair reads), fetched with
-//               cp.async; sequences too long for it fall back to a per-block slab the producer
-//               writes;
+//               128-bit loads; sequences too long for it fall back to a per-block slab the
+//               producer writes;
 //   warp 1      TMEM owner (512 columns) and the single-thread tcgen05.mma issuer:
 //               S_t = Q_t K^T (SS, K = DP) into TMEM, O_t += P_t V (TS: P read from TMEM, one
 //               N = DP instruction per 16 keys);
@@ -85,10 +85,7 @@ constexpr int kRowPad = 256;
 __host__ __device__ constexpr int64_t row_floats(int64_t S) { return (2 * S - 1 + kRowPad + 128 + 1) / 2 * 2; }
 __host__ __device__ constexpr int64_t row_bytes(int64_t S) { return 2 * row_floats(S) * 4; }
 
-__device__ __forceinline__ void cp_async4(float* smem_dst, const float* gsrc) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 
 template <int DP, bool F16, bool RES>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -181,23 +178,13 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
     }
   } else if (warp == 2 || warp == 3) {
     // ------------------------------------------------------------ resident bias rows (RES)
-    // cp.async keeps every load of the row in flight at once; each thread then scales its own
-    // elements by log2(e) (its copies have landed after wait_all) and arrives.
     if constexpr (RES) {
       const int two_s = 2 * a.S - 1;
       const float* pdh = a.pd + (size_t)h * two_s;
       const int n = (int)row_floats(a.S);
       const int tid = threadIdx.x - 64;
-      for (int i = tid; i < n; i += 64) {
-        const int pos = i - kRowPad;
-        if (pos >= 0 && pos < two_s) cp_async4(row0 + i, pdh + pos); else row0[i] = 0.f;
-        if (pos + 1 >= 0 && pos + 1 < two_s) cp_async4(row1 + i, pdh + pos + 1); else row1[i] = 0.f;
-      }
-      cp_async_wait_all();
-      for (int i = tid; i < n; i += 64) {
-        row0[i] *= kLog2e;
-        row1[i] *= kLog2e;
-      }
+      attn::fill_row(row0, n, kRowPad, pdh, two_s, kLog2e, tid, 64);
+      attn::fill_row(row1, n, kRowPad - 1, pdh, two_s, kLog2e, tid, 64);   // row1[i] = row0[i + 1]
       mbar_arrive(row_full);
     }
   } else if (warp == 1) {
