@@ -71,6 +71,23 @@ int krsi_rmsnorm_bwd(const void* g, const void* x, const void* w, const float* r
                      void* dx, void* dw, void* workspace, size_t workspace_bytes,
                      int64_t rows, int64_t n, int x_dtype, int w_dtype, cudaStream_t stream);
 
+/* The same backward for callers that cannot allocate device memory (a host that owns all device
+ * memory, or a loop that must not stall on cudaMalloc): the dw partial sums live in a fixed
+ * device array inside this library (4 MiB per GPU that loads it, kept until the process exits)
+ * instead of a caller workspace.  No counterpart in the reference (its backward allocates
+ * through torch, rmsnorm.py:93).
+ * Limit: (dw partial rows) x n <= 1,048,576 floats.  The partial-row count is
+ * min(ceil(rows / 8), 296) when one warp handles a row (rows of up to 2048 fp32 or 4096
+ * 16-bit elements, 16-byte aligned) and min(rows, 296) otherwise; for example rows = 2048,
+ * n = 1152 uses 256 x 1152.  Larger problems return KRSI_ERR_UNSUPPORTED.
+ * The first call on each device looks up the array's address (cudaGetSymbolAddress) with that
+ * device current; make that first call before any stream capture.  All calls share the array:
+ * calls whose kernels overlap on the GPU (different streams, same device) race and corrupt dw.
+ * Allocates nothing: no cudaMalloc, cudaFree or allocating library call. */
+int krsi_rmsnorm_bwd_noalloc(const void* g, const void* x, const void* w, const float* rstd,
+                             void* dx, void* dw, int64_t rows, int64_t n, int x_dtype, int w_dtype,
+                             cudaStream_t stream);
+
 /* ---------------------------------------------------------------- GEGLU
  * out = gelu_tanh(u[:, :F]).to(dtype) * u[:, F:].
  * Replaces library/geglu.py:209-215 (_fwd -> _geglu_fwd, geglu.py:181-189).

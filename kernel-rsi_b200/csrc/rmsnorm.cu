@@ -12,6 +12,8 @@
 // VEC elements at columns (c*TPR + t)*VEC, so each load/store instruction of a row group is
 // one fully coalesced 128-bit-per-thread transaction.  NCH is a compile-time constant, so
 // the row slice stays in registers.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace krsi {
@@ -407,4 +409,67 @@ extern "C" int krsi_rmsnorm_bwd(const void* g, const void* x, const void* w, con
   if (!workspace || workspace_bytes < (size_t)nblocks * (size_t)n * sizeof(float)) return KRSI_ERR_WORKSPACE;
   return dispatch<false>(x_dtype, w_dtype, p,
                          BwdArgs{g, x, w, rstd, dx, dw, static_cast<float*>(workspace), nblocks, rows, (int)n, stream});
+}
+
+// ---------------------------------------------------------------- allocation-free backward
+// Some callers cannot allocate device memory at the point where they run the backward: hosts
+// that own every device allocation themselves (an embedding framework with its own pool), code
+// that runs while other work holds the allocator, or real-time loops where a cudaMalloc would
+// stall the device.  krsi_rmsnorm_bwd_noalloc gives them the same kernels with the dweight
+// partial sums placed in a fixed, file-scope device array instead of a caller workspace.
+namespace krsi {
+namespace {
+
+constexpr int64_t kNoAllocScratchFloats = 1 << 20;   // 4 MiB: (dw partial rows) x n <= 1,048,576
+// One copy per GPU that loads this library, alive until the process exits.  Host code may not use
+// the symbol as a pointer (it names a host-side stand-in): its device address is looked up per
+// device with cudaGetSymbolAddress.
+static __device__ __align__(256) float g_rms_noalloc_scratch[kNoAllocScratchFloats];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+float* g_scratch_ptr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device, looked up once per device.
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  KRSI_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return KRSI_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    KRSI_CUDA_TRY(cudaGetSymbolAddress(&p, g_rms_noalloc_scratch));
+    g_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_scratch_ptr[dev];
+  return KRSI_OK;
+}
+
+}  // namespace
+}  // namespace krsi
+
+extern "C" int krsi_rmsnorm_bwd_noalloc(const void* g, const void* x, const void* w, const float* rstd, void* dx,
+                                        void* dw, int64_t rows, int64_t n, int x_dtype, int w_dtype,
+                                        cudaStream_t stream) {
+  KRSI_CHECK_ARG(rows >= 0 && n >= 0 && dtype_ok(x_dtype) && dtype_ok(w_dtype));
+  if (n == 0) return KRSI_OK;
+  KRSI_CHECK_ARG(w && dw);
+  if (n > 0x7fffffff) return KRSI_ERR_UNSUPPORTED;
+  if (rows == 0) {  // dw of an empty batch is zero
+    KRSI_CUDA_TRY(cudaMemsetAsync(dw, 0, (size_t)n * elem_size(w_dtype), stream));
+    return KRSI_OK;
+  }
+  KRSI_CHECK_ARG(g && x && rstd && dx);
+  const int vw = 16 / elem_size(x_dtype);
+  const bool vec_ok = (n % vw == 0) && aligned16(x) && aligned16(g) && aligned16(dx) && aligned16(w);
+  Plan p;
+  if (!plan_rows(n, x_dtype, vec_ok, &p)) return KRSI_ERR_UNSUPPORTED;
+  const int64_t nblocks = bwd_blocks(rows, p);
+  if (nblocks * n > kNoAllocScratchFloats) return KRSI_ERR_UNSUPPORTED;   // beyond the fixed scratch
+  float* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != KRSI_OK) return rc;
+  // Every partial row the reduction reads is written by this launch first, so the array's
+  // previous contents never leak into the result and nothing needs clearing.
+  return dispatch<false>(x_dtype, w_dtype, p, BwdArgs{g, x, w, rstd, dx, dw, scratch, nblocks, rows, (int)n, stream});
 }
