@@ -710,7 +710,8 @@ def main():
         from datetime import timedelta
 
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0))))
     try:
         if args.impl == "reference":
             run_reference_arm(args, rank, world)
