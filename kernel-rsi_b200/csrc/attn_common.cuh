@@ -90,6 +90,42 @@ __device__ __forceinline__ void fill_row(float* dst, int n, int pad, const float
   }
 }
 
+// Fills dst[i] = src[top - i] * mul for i in [0, n), zero where top - i is outside [lo, hi] (a
+// reversed window of src; lo >= 0 and hi must be valid source indices or lo > hi).  Same
+// cooperative scheme as fill_row: the 16-byte-aligned interior of src[lo..hi] is read with 128-bit
+// loads (four in flight per thread) and scattered in reverse order.
+__device__ __forceinline__ void fill_row_rev(float* dst, int n, int top, const float* __restrict__ src, int lo, int hi,
+                                             float mul, int tid, int nthr) {
+  const int len = hi >= lo ? hi - lo + 1 : 0;
+  const int mis = (int)((reinterpret_cast<uintptr_t>(src + lo) >> 2) & 3);
+  const int a0 = lo + (mis ? min(4 - mis, len) : 0);   // first aligned source index
+  const int nvec = lo + len > a0 ? (lo + len - a0) / 4 : 0;
+  const int a1 = a0 + 4 * nvec;
+  const float4* src4 = reinterpret_cast<const float4*>(src + a0);
+  for (int v0 = tid; v0 < nvec; v0 += 4 * nthr) {
+    float4 x[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (v0 + u * nthr < nvec) x[u] = __ldg(src4 + v0 + u * nthr);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int m = a0 + 4 * (v0 + u * nthr);   // source index of x[u].x
+      const int i = top - m;                      // its destination; m + 1.. go to i - 1..
+      if (v0 + u * nthr < nvec) {
+        if (i >= 0 && i < n) dst[i] = x[u].x * mul;
+        if (i - 1 >= 0 && i - 1 < n) dst[i - 1] = x[u].y * mul;
+        if (i - 2 >= 0 && i - 2 < n) dst[i - 2] = x[u].z * mul;
+        if (i - 3 >= 0 && i - 3 < n) dst[i - 3] = x[u].w * mul;
+      }
+    }
+  }
+  for (int i = tid; i < n; i += nthr) {
+    const int m = top - i;
+    if (m < lo || m > hi) dst[i] = 0.f;
+    else if (m < a0 || m >= a1) dst[i] = __ldg(src + m) * mul;
+  }
+}
+
 // ---------------------------------------------------------------- host side
 using EncodeTiledFn = PFN_cuTensorMapEncodeTiled_v12000;
 
@@ -120,6 +156,24 @@ inline bool make_head_map(CUtensorMap* map, const void* base, int64_t row_stride
   CUresult r = enc(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// 3-D fp32 view (D, S, B) of head `h` columns of a [B*S, n_heads*D] fp32 tensor, for the TMA
+// reduce-add of a [128 rows x D] tile: element (d, s, b) at base + ((b*S + s)*n_heads*D + d), the
+// caller adds h*D to the x coordinate.  Box = (D, 128, 1), no swizzle (row-major tile with a D*4-byte
+// pitch).  Rows >= S are clipped, so a ragged last block writes nothing outside its batch.
+inline bool make_rows_f32_map(CUtensorMap* map, float* base, int64_t B, int64_t S, int64_t n_heads, int64_t D) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  memset(map, 0, sizeof(*map));
+  cuuint64_t dims[3] = {(cuuint64_t)(n_heads * D), (cuuint64_t)S, (cuuint64_t)B};
+  cuuint64_t strides[2] = {(cuuint64_t)(n_heads * D * 4), (cuuint64_t)(S * n_heads * D * 4)};
+  cuuint32_t box[3] = {(cuuint32_t)D, (cuuint32_t)kTileRows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 

@@ -8,18 +8,24 @@
 //
 // Kernels:
 //   bwd_prep   delta from dO and O32; zeroes the fp32 dQ accumulator.
-//   bwd_main   one CTA per (b*H + h, 128-key block); loops over the 128-query blocks:
-//                warp 0     TMA producer: K and V once; Q, dO tiles + lse/delta/bias slab
-//                           per query block (2-stage ring)
-//                warp 1     TMEM owner + tcgen05.mma issuer:
-//                             S^T = K Q^T, dP^T = V dO^T              (SS, K = DP)
-//                             dV += P^T dO, dK += dS^T Q               (TS: P^T/dS^T in TMEM)
-//                             dQ  = dS K                              (SS: dS staged in smem)
-//                warps 2-5  one key row per thread: P^T, dS^T (fp32) -> bf16 into TMEM and
-//                           smem; dBias diagonal sums of the fp32 dS tile by a warp-shuffle
-//                           scan, written as one 255-vector per tile (no S x S buffer)
-//                warps 6-9  one query row per thread: dQ tile from TMEM -> fp32 vector
-//                           reductions into the accumulator; at the end dK, dV -> dqkv
+//   bwd_main   one CTA per (b*H + h, 128-key block); loops over the 128-query blocks with four
+//              warpgroups:
+//                warp 0      TMA producer: K and V once; Q and dO tiles per query block (2 stages)
+//                            and the block's -lse, -delta (and bias slab when not resident)
+//                warp 1      TMEM owner + tcgen05.mma issuer, software-pipelined so the next
+//                            block's S^T is computed while the current dS is:
+//                              S^T = K Q^T, dP^T = V dO^T              (SS, K = DP)
+//                              dV += P^T dO, dK += dS^T Q               (TS: P^T/dS^T in TMEM)
+//                              dQ  = dS K                              (SS: dS staged in smem)
+//                warps 2-3   (with warps 12-15) the resident bias rows: a reversed window of the
+//                            bias row, in two copies (the second shifted by one, for aligned pairs)
+//                warps 4-11  two compute warpgroups, one key row per thread and 64 queries per
+//                            warpgroup: P^T, dS^T in paired fp32 -> 16-bit into TMEM and smem;
+//                            dBias diagonal sums of the fp32 dS by a warp-shuffle transpose into
+//                            per-lane register bins (no S x S buffer, no atomics)
+//                warps 12-15 one query row per thread: dQ tile from TMEM -> a shared-memory tile
+//                            that one TMA reduce-add sums into the fp32 accumulator; at the end
+//                            dK, dV -> dqkv
 //   bwd_dq     dQ accumulator * scale -> dqkv (input dtype)
 //   bwd_dpd    dpd[h, t] = fixed-order sum of the per-tile diagonal partials (deterministic)
 // dK, dV and dpd are bitwise reproducible; dQ sums per-key-block fp32 partials in arrival
@@ -42,14 +48,17 @@ namespace {
 using namespace sm100;
 using attn::kTileRows;
 
-constexpr int kBlk = 128;          // keys per CTA, queries per iteration
-constexpr int kThreads = 384;       // 3 warpgroups: {producer, MMA, -, -}, compute, dQ/epilogue
-constexpr uint32_t kRegsCtl = 96;   // after setmaxnreg (launch 168 x 384 = 128 x (96 + 248 + 160))
-constexpr uint32_t kRegsCompute = 248;
-constexpr uint32_t kRegsDq = 160;
-constexpr int kBins = 160;          // per-warp diagonal bins: 32 keys x 128 queries -> 159 diagonals
-constexpr int kDiag = 2 * kBlk - 1;     // 255 diagonals per 128 x 128 tile
-
+constexpr int kBlk = 128;           // keys per CTA, queries per iteration
+constexpr int kHalf = 64;           // queries per compute warpgroup
+constexpr int kThreads = 512;       // 4 warpgroups: control, compute (queries 0-63, 64-127), dQ/epilogue
+// setmaxnreg budgets: the launch holds 128 registers x 512 threads = 65,536, and
+// 128 x (104 + 160 + 160 + 88) = 65,536 are handed out, so every increase can be satisfied.
+constexpr uint32_t kRegsCtl = 104;
+constexpr uint32_t kRegsCompute = 160;
+constexpr uint32_t kRegsDq = 88;
+constexpr int kWarpsPerTile = 8;    // dBias partial rows per tile: (query half, key quarter)
+constexpr int kBins = 96;           // per-warp bins: 32 keys x 64 queries -> 95 diagonals (+1 zero)
+constexpr int kRowFillers = 192;    // warps 2-3 and 12-15 fill the resident rows
 
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -61,13 +70,16 @@ struct BwdCfg {
   static constexpr uint32_t kVOff = kKOff + kTile;
   static constexpr uint32_t kQOff = kVOff + kTile;                // stage s: Q at kQOff + s*2*kTile
   static constexpr uint32_t kDSOff = kQOff + NQS * 2 * kTile;     // dS (bf16, MN-major SW128): 2 x 16 KB
-  static constexpr uint32_t kVecOff = kDSOff + 2 * 16384;         // per stage: lse[128], delta[128], slab[256]
-  static constexpr uint32_t kVecBytes = (128 + 128 + 256) * 4;
+  static constexpr uint32_t kStgOff = kDSOff + 2 * 16384;          // dQ tile staging: 128 rows x D fp32
+  // per stage: -lse[128], -delta[128] and (bias not resident) the reversed bias slab [256] with its
+  // copy shifted by one element [256]
+  static constexpr uint32_t kVecOff = kStgOff + kTileRows * DP * 4;
+  static constexpr uint32_t kVecBytes = (128 + 128 + 2 * 256) * 4;
   static constexpr uint32_t kBarOff = kVecOff + NQS * kVecBytes;
-  static constexpr int kNumBars = 1 + 2 * NQS + 8;
+  static constexpr int kNumBars = 1 + 2 * NQS + 11;
   static constexpr uint32_t kMiscOff = kBarOff + kNumBars * 8;
-  static constexpr uint32_t kRowOff = kMiscOff + 16;   // resident pd / lse / delta rows (runtime length)
-  static constexpr uint32_t kSmem = kRowOff + 1024;
+  static constexpr uint32_t kRowOff = (kMiscOff + 16 + 15) & ~15u;   // resident rows (runtime length)
+  static constexpr uint32_t kSmem = kRowOff + 1024;                  // + the 1 KB alignment slack
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kST = 0, kDPT = 128, kDV = 256, kDK = 256 + DP, kDQ = 256 + 2 * DP;
   static_assert(kDQ + DP <= kTmemCols, "backward TMEM plan needs DP <= 80");
@@ -77,8 +89,8 @@ struct BwdArgs {
   const float* pd;
   const float* lse;
   const float* delta;
-  float* dq_acc;          // [B*S, H*D] fp32
-  float* dbias_part;      // [B*H, n_kb, n_qb, 4 warps, kBins]
+  float* dq_acc;          // [B*S, H*D] fp32 (the main kernel adds into it through its tensor map)
+  float* dbias_part;      // [B*H, n_kb, n_qb, kWarpsPerTile, kBins]
   void* dqkv;
   int64_t dqkv_stride;
   int B, S, H, D, n_blk;
@@ -86,24 +98,27 @@ struct BwdArgs {
   uint32_t spin_limit;
 };
 
-__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
+// TMEM column of the 16-bit P^T / dS^T pairs of queries [16 kk, 16 kk + 16): each compute
+// warpgroup packs its 64 queries into the first 32 of its own 64 fp32 columns, so neither
+// overwrites columns the other has yet to read.
+__host__ __device__ constexpr uint32_t packed_col(int kk) { return kk * 8 + (kk >= kHalf / 16 ? kHalf / 2 : 0); }
+
+// Resident bias rows (one load per CTA).  The bias of (key, query) is pd[h, key - query + S - 1]; the
+// keys of CTA kb and all padded queries [0, nb*128) use m in [m_top - (nb*128 + 126), m_top] with
+// m_top = k0 + 127 + S - 1.  The row stores that window reversed and scaled by log2(e):
+//   rev[kRevPad + t] = pd[h, m_top - t] * log2e   (zero outside [0, 2S-2]),
+// so bias(k0 + kr, q) = rev[kRevPad + 127 - kr + q] ascends with the query, and a second copy
+// shifted by one element (rev1[i] = rev[i + 1]) makes every pair of queries an aligned 8-byte read.
+constexpr int kRevPad = 4;
+__host__ __device__ constexpr int64_t rev_row_floats(int64_t S) {
+  return ((kRevPad + ((S + kBlk - 1) / kBlk) * kBlk + kBlk + 4) + 3) & ~int64_t(3);
 }
-
-
-// Resident rows (one load per CTA): pd[h, :] * log2(e) with kRowPad zeros before and 128 after
-// (every key - query + S - 1 a tile forms stays inside), then lse and delta of this (b, h), each
-// followed by 128 zeros for queries past S.
-constexpr int kRowPad = 256;
-__host__ __device__ constexpr int64_t pd_row_floats(int64_t S) { return 2 * S - 1 + kRowPad + 128; }
-__host__ __device__ constexpr int64_t vec_row_floats(int64_t S) { return S + 128; }
-__host__ __device__ constexpr int64_t rows_bytes(int64_t S) { return (pd_row_floats(S) + 2 * vec_row_floats(S)) * 4; }
+__host__ __device__ constexpr int64_t rows_bytes(int64_t S) { return 2 * rev_row_floats(S) * 4; }
 
 template <int DP, bool F16, bool RES>
 __global__ void __launch_bounds__(kThreads, 1)
 relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap omap,
-                       const BwdArgs a) {
+                       const __grid_constant__ CUtensorMap dqmap, const BwdArgs a) {
   using C = BwdCfg<DP>;
   constexpr int NQS = C::NQS;
   extern __shared__ uint8_t smem_raw[];
@@ -112,17 +127,19 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
   uint64_t* kv_full = bars;
   uint64_t* qdo_full = bars + 1;
   uint64_t* qdo_empty = bars + 1 + NQS;
-  uint64_t* sdp_ready = bars + 1 + 2 * NQS;
-  uint64_t* p_ready = sdp_ready + 1;
-  uint64_t* ds_ready = sdp_ready + 2;
-  uint64_t* dq_ready = sdp_ready + 3;
-  uint64_t* dq_free = sdp_ready + 4;
-  uint64_t* kdv_done = sdp_ready + 5;
-  uint64_t* drain = sdp_ready + 6;
-  uint64_t* row_full = sdp_ready + 7;
-  float* pd_row = reinterpret_cast<float*>(smem + C::kRowOff);
-  float* lse_row = pd_row + pd_row_floats(a.S);
-  float* del_row = lse_row + vec_row_floats(a.S);
+  uint64_t* s_ready = bars + 1 + 2 * NQS;   // S^T of the current block in TMEM
+  uint64_t* dp_ready = s_ready + 1;          // dP^T of the current block in TMEM
+  uint64_t* p_ready = s_ready + 2;           // P^T written (256 compute threads)
+  uint64_t* ds_ready = s_ready + 3;          // dS^T written to TMEM and smem (256)
+  uint64_t* dq_ready = s_ready + 4;
+  uint64_t* dq_free = s_ready + 5;
+  uint64_t* kdv_done = s_ready + 6;
+  uint64_t* drain = s_ready + 7;
+  uint64_t* row_full = s_ready + 8;
+  uint64_t* stg_free = s_ready + 9;          // dQ staging tile read by the previous reduce-add (leader)
+  uint64_t* stg_full = s_ready + 10;         // dQ staging tile written (128 dQ threads)
+  float* rev0 = reinterpret_cast<float*>(smem + C::kRowOff);
+  float* rev1 = rev0 + rev_row_floats(a.S);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
 
@@ -134,17 +151,20 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
     for (int s = 0; s < NQS; ++s) {
-      mbar_init(&qdo_full[s], RES ? 1 : 2);   // TMA expect_tx (+ vectors/slab stores)
+      mbar_init(&qdo_full[s], 2);   // TMA expect_tx + the producer's vectors
       mbar_init(&qdo_empty[s], 1);
     }
-    mbar_init(sdp_ready, 1);
-    mbar_init(p_ready, 128);
-    mbar_init(ds_ready, 128);
+    mbar_init(s_ready, 1);
+    mbar_init(dp_ready, 1);
+    mbar_init(p_ready, 2 * 128);
+    mbar_init(ds_ready, 2 * 128);
     mbar_init(dq_ready, 1);
     mbar_init(dq_free, 128);
     mbar_init(kdv_done, 1);
     mbar_init(drain, 1);
-    mbar_init(row_full, 64);
+    mbar_init(row_full, kRowFillers);
+    mbar_init(stg_free, 1);
+    mbar_init(stg_full, 128);
     abort_flag[0] = 0;
     abort_flag[1] = 0;
     fence_barrier_init();
@@ -152,6 +172,7 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
   if (warp == 0 && lane == 0) {
     prefetch_tensormap(&qmap);
     prefetch_tensormap(&omap);
+    prefetch_tensormap(&dqmap);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -161,6 +182,19 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+
+  // Resident bias rows, filled cooperatively by warps 2-3 and 12-15 (192 threads).
+  auto fill_rows = [&](int tid) {
+    const int two_s = 2 * a.S - 1;
+    const float* pdh = a.pd + (size_t)h * two_s;
+    const int m_top = k0 + kBlk - 1 + a.S - 1;
+    const int n = (int)rev_row_floats(a.S);
+    const int top = m_top + kRevPad;   // rev[i] = pd[top - i]
+    const int lo = max(0, m_top - (nq * kBlk + kBlk - 2)), hi = min(two_s - 1, m_top);
+    attn::fill_row_rev(rev0, n, top, pdh, lo, hi, kLog2e, tid, kRowFillers);
+    attn::fill_row_rev(rev1, n, top - 1, pdh, lo, hi, kLog2e, tid, kRowFillers);
+    mbar_arrive(row_full);
+  };
 
   // Each role runs entirely inside the branch that sets its register budget.
   if (warp < 4) {
@@ -190,32 +224,27 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
         attn::load_tile<DP>(qt, &qmap, &qdo_full[s], h, q0, b);
         attn::load_tile<DP>(qt + C::kTile, &omap, &qdo_full[s], h, q0, b);
       }
-      if constexpr (RES) continue;
       float* vec = reinterpret_cast<float*>(smem + C::kVecOff + s * C::kVecBytes);
       for (int r = lane; r < kBlk; r += 32) {
         const int q = q0 + r;
-        vec[r] = q < a.S ? __ldg(lse_bh + q) : 0.f;
-        vec[128 + r] = q < a.S ? __ldg(del_bh + q) : 0.f;
+        vec[r] = q < a.S ? -__ldg(lse_bh + q) : 0.f;
+        vec[128 + r] = q < a.S ? -__ldg(del_bh + q) : 0.f;
       }
-      // slab[t] = pd[h, k0 - q0 - 127 + t + S - 1] * log2e for t in [0, 255)
-      const int base = k0 - q0 - (kBlk - 1) + a.S - 1;
+      if constexpr (!RES) {
+      // slab[t] = pd[h, k0 - q0 + 127 - t + S - 1] * log2e for t in [0, 255), so that
+      // bias(k0 + kr, q0 + q) = slab[127 - kr + q]; slab1[t] = slab[t + 1]
+      const int top = k0 - q0 + kBlk - 1 + a.S - 1;
       for (int t = lane; t < 256; t += 32) {
-        const int pos = base + t;
-        vec[256 + t] = (t < kDiag && pos >= 0 && pos < two_s) ? __ldg(pdh + pos) * kLog2e : 0.f;
+        const int pos = top - t;
+        vec[256 + t] = (t < 2 * kBlk - 1 && pos >= 0 && pos < two_s) ? __ldg(pdh + pos) * kLog2e : 0.f;
+        vec[512 + t] = (t + 1 < 2 * kBlk - 1 && pos - 1 >= 0 && pos - 1 < two_s) ? __ldg(pdh + pos - 1) * kLog2e : 0.f;
+      }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&qdo_full[s]);
     }
   } else if (warp == 2 || warp == 3) {
-    // ------------------------------------------------------------ resident rows (RES)
-    if constexpr (RES) {
-      const int tid = threadIdx.x - 64;
-      const int two_s = 2 * a.S - 1;
-      attn::fill_row(pd_row, (int)pd_row_floats(a.S), kRowPad, a.pd + (size_t)h * two_s, two_s, kLog2e, tid, 64);
-      attn::fill_row(lse_row, (int)vec_row_floats(a.S), 0, a.lse + (size_t)bh * a.S, a.S, 1.f, tid, 64);
-      attn::fill_row(del_row, (int)vec_row_floats(a.S), 0, a.delta + (size_t)bh * a.S, a.S, 1.f, tid, 64);
-      mbar_arrive(row_full);
-    }
+    if constexpr (RES) fill_rows(threadIdx.x - 64);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -235,33 +264,52 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
       const uint64_t ds_d = smem_desc(smem_u32(smem + C::kDSOff), 16384, 1024, kSw128);
       constexpr uint64_t kStage = (2 * C::kTile) >> 4;
       constexpr uint64_t kDsRows = (16 * 128) >> 4;   // next 16 keys of dS
-      bool ok = mbar_wait_bounded(kv_full, 0, abort_flag, a.spin_limit);
-      for (int i = 0; i < nq && ok; ++i) {
-        const int s = i % NQS;
-        const uint64_t so = (uint64_t)s * kStage;
-        if (!mbar_wait_bounded(&qdo_full[s], (i / NQS) & 1, abort_flag, a.spin_limit)) { ok = false; break; }
+      auto issue_s = [&](int s) {        // S^T = K Q^T (rows = keys)
+#pragma unroll
+        for (int kk = 0; kk < DP / 16; ++kk)
+          mma_ss(tmem + C::kST, k_kd + kk * attn::kKSliceStep, q_kd0 + s * kStage + kk * attn::kKSliceStep, id_sq,
+                 kk > 0);
+      };
+      auto issue_dp = [&](int s) {       // dP^T = V dO^T
+#pragma unroll
+        for (int kk = 0; kk < DP / 16; ++kk)
+          mma_ss(tmem + C::kDPT, v_kd + kk * attn::kKSliceStep, o_kd0 + s * kStage + kk * attn::kKSliceStep, id_sq,
+                 kk > 0);
+      };
+      // Order per block i (in-order tensor pipe, so every overwrite follows the reads before it):
+      //   [P_i] dV_i, S_{i+1} -> s_ready   [dS_i] dK_i, dQ_i, dP_{i+1} -> dp_ready
+      bool ok = mbar_wait_bounded(kv_full, 0, abort_flag, a.spin_limit) &&
+                mbar_wait_bounded(&qdo_full[0], 0, abort_flag, a.spin_limit);
+      if (ok) {
         tc_fence_after();
-        // S^T = K Q^T and dP^T = V dO^T (rows = keys)
-#pragma unroll
-        for (int kk = 0; kk < DP / 16; ++kk)
-          mma_ss(tmem + C::kST, k_kd + kk * attn::kKSliceStep, q_kd0 + so + kk * attn::kKSliceStep, id_sq, kk > 0);
-#pragma unroll
-        for (int kk = 0; kk < DP / 16; ++kk)
-          mma_ss(tmem + C::kDPT, v_kd + kk * attn::kKSliceStep, o_kd0 + so + kk * attn::kKSliceStep, id_sq, kk > 0);
-        mma_commit(sdp_ready);
+        issue_s(0);
+        mma_commit(s_ready);
+        issue_dp(0);
+        mma_commit(dp_ready);
+      }
+      for (int i = 0; i < nq && ok; ++i) {
+        const int s = i % NQS, s1 = (i + 1) % NQS;
+        const uint64_t so = (uint64_t)s * kStage;
         const uint32_t acc0 = i > 0 ? 1u : 0u;
-        // dV += P^T dO
+        const bool next = i + 1 < nq;
+        // dV += P^T dO, then the next block's S^T
         if (!mbar_wait_bounded(p_ready, i & 1, abort_flag, a.spin_limit)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kBlk / 16; ++kk)
-          mma_ts(tmem + C::kDV, tmem + C::kST + kk * 8, o_mn0 + so + kk * attn::kKRowStep, id_nd, kk > 0 ? 1u : acc0);
-        // dK += dS^T Q, then dQ = dS K (dQ's TMEM columns must have been drained)
+          mma_ts(tmem + C::kDV, tmem + C::kST + packed_col(kk), o_mn0 + so + kk * attn::kKRowStep, id_nd, kk > 0 ? 1u : acc0);
+        if (next) {
+          if (!mbar_wait_bounded(&qdo_full[s1], ((i + 1) / NQS) & 1, abort_flag, a.spin_limit)) { ok = false; break; }
+          tc_fence_after();
+          issue_s(s1);
+          mma_commit(s_ready);
+        }
+        // dK += dS^T Q, dQ = dS K (dQ's TMEM columns drained), then the next block's dP^T
         if (!mbar_wait_bounded(ds_ready, i & 1, abort_flag, a.spin_limit)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kBlk / 16; ++kk)
-          mma_ts(tmem + C::kDK, tmem + C::kDPT + kk * 8, q_mn0 + so + kk * attn::kKRowStep, id_nd, kk > 0 ? 1u : acc0);
+          mma_ts(tmem + C::kDK, tmem + C::kDPT + packed_col(kk), q_mn0 + so + kk * attn::kKRowStep, id_nd, kk > 0 ? 1u : acc0);
         if (i > 0 && !mbar_wait_bounded(dq_free, (i - 1) & 1, abort_flag, a.spin_limit)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
@@ -269,6 +317,10 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
           mma_ss(tmem + C::kDQ, ds_d + kk * kDsRows, k_mn + kk * attn::kKRowStep, id_dq, kk > 0 ? 1u : 0u);
         mma_commit(dq_ready);
         mma_commit(&qdo_empty[s]);
+        if (next) {
+          issue_dp(s1);
+          mma_commit(dp_ready);
+        }
       }
       if (ok) mma_commit(kdv_done);
       else watchdog_fire(kWdBwdMma);
@@ -278,88 +330,115 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
       }
     }
   }
-  } else if (warp < 8) {
+  } else if (warp < 12) {
     regs_inc<kRegsCompute>();
-    // ------------------------------------------------------------ compute WG: one key per thread
-    const int quarter = warp % 4;
+    // ------------------------------------------------------------ compute: one key x 64 queries per thread
+    const int quarter = warp % 4, half = (warp - 4) / 4;
     const int kr = quarter * 32 + lane;        // key row within the block (TMEM lane)
-    const int key = k0 + kr;
-    const bool key_ok = key < a.S;
+    const int qh = half * kHalf;               // first query of this warpgroup within the block
+    const bool key_ok = k0 + kr < a.S;
+    const bool keys_full = k0 + kBlk <= a.S;
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
     const uint32_t st_t = tmem + lane_addr + C::kST;
     const uint32_t dpt_t = tmem + lane_addr + C::kDPT;
-    uint8_t* ds_smem = smem + C::kDSOff;
-    // dBias: this warp's 32 keys x 128 queries of dS touch 159 diagonals ("bins"): bin j holds
-    // key - query = 32 * quarter + 31 - j within the tile.  Each 32 x 32 sub-tile is transposed
-    // along its diagonals by 32 independent shuffles (lane l reads dS[(l + m) & 31][m]), so lane l
-    // owns bins 31 - l + 32 k (k = 0..4) and sums them in registers in a fixed order:
+    uint8_t* ds_row = smem + C::kDSOff + half * 16384 + kr * 128;   // this key's row of the dS atom
+    const uint64_t scale2 = f2_pack(a.scale_log2, a.scale_log2);
+    // dBias: this warp's 32 keys x 64 queries of dS touch 95 diagonals ("bins"): bin j holds
+    // key - query = 32 * quarter - 64 * half + 31 - j within the tile.  Each 32 x 32 sub-tile is
+    // transposed along its diagonals by 32 independent shuffles (lane l reads dS[(l + m) & 31][m]),
+    // so lane l owns bins 31 - l + 32 k (k = 0..2) and sums them in registers in a fixed order:
     // deterministic, no atomics, no serial chain.
     bool ok = !RES || __all_sync(0xffffffffu, mbar_wait_bounded(row_full, 0, abort_flag, a.spin_limit));
     for (int i = 0; i < nq && ok; ++i) {
       const int s = i % NQS;
       const int q0 = i * kBlk;
-      const bool w_ok = mbar_wait_bounded(sdp_ready, i & 1, abort_flag, a.spin_limit) &&
-                        (RES || mbar_wait_bounded(&qdo_full[s], (i / NQS) & 1, abort_flag, a.spin_limit));
+      const bool w_ok = mbar_wait_bounded(s_ready, i & 1, abort_flag, a.spin_limit) &&
+                        mbar_wait_bounded(&qdo_full[s], (i / NQS) & 1, abort_flag, a.spin_limit);
       if (!__all_sync(0xffffffffu, w_ok)) {   // warp-uniform: TMEM ops below are warp-collective
         ok = false;
         break;
       }
       tc_fence_after();
       const float* vec = reinterpret_cast<const float*>(smem + C::kVecOff + s * C::kVecBytes);
-      const float* lse_p = RES ? lse_row + q0 : vec;
-      const float* del_p = RES ? del_row + q0 : vec + 128;
-      // bias(key, q0 + q) = slab[-q]
-      const float* slab = RES ? pd_row + kRowPad + key - q0 + a.S - 1 : vec + 256 + kr + (kBlk - 1);
-      const int qvalid = a.S - q0;
-      float p[kBlk];
+      const ulonglong2* nlse2 = reinterpret_cast<const ulonglong2*>(vec + qh);
+      const ulonglong2* ndel2 = reinterpret_cast<const ulonglong2*>(vec + 128 + qh);
+      // bias(key, q0 + qh + q) = bq[q], read as aligned pairs from whichever copy makes them aligned
+      const int bbase = RES ? kRevPad + kBlk - 1 - kr + q0 + qh : kBlk - 1 - kr + qh;
+      const float* c0 = RES ? rev0 : vec + 256;
+      const float* c1 = RES ? rev1 : vec + 512;
+      const uint64_t* bq2 = reinterpret_cast<const uint64_t*>((bbase & 1) ? c1 + bbase - 1 : c0 + bbase);
+      const bool full = keys_full && q0 + kBlk <= a.S;
+      const int qvalid = a.S - q0 - qh;        // queries of this warpgroup inside the sequence
+
+      // P^T = exp2(s2 - lse) in paired fp32; 16-bit copy over S^T in TMEM
+      uint64_t p2[kHalf / 2];
       {
-        uint32_t* u = reinterpret_cast<uint32_t*>(p);
-#pragma unroll
-        for (int c = 0; c < kBlk; c += 32) tmem_ld32(st_t + c, u + c);
+        uint32_t u[kHalf];
+        tmem_ld32(st_t + qh, u);
+        tmem_ld32(st_t + qh + 32, u + 32);
         tmem_wait_ld();
-      }
-      // P^T = exp2(s2 - lse), zero outside the sequence; bf16/f16 copy over S^T in TMEM
+        uint32_t pk[kHalf / 2];
 #pragma unroll
-      for (int qc = 0; qc < kBlk / 32; ++qc) {
-        uint32_t pk[16];
+        for (int j = 0; j < kHalf / 4; ++j) {
+          const ulonglong2 nl = nlse2[j];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int q = qc * 32 + e;
-          const float s2 = fmaf(p[q], a.scale_log2, slab[-q]) - lse_p[q];
-          p[q] = (key_ok && q < qvalid) ? ex2_approx(s2) : 0.f;
-          if (e & 1) pk[e / 2] = F16 ? pack_f16x2(p[q - 1], p[q]) : pack_bf16x2(p[q - 1], p[q]);
+          for (int t = 0; t < 2; ++t) {
+            const int e = 2 * j + t;   // pair index: queries 2e, 2e + 1
+            uint64_t x = f2_fma(f2_pack(__uint_as_float(u[2 * e]), __uint_as_float(u[2 * e + 1])), scale2, bq2[e]);
+            x = f2_add(x, t ? nl.y : nl.x);
+            float x0, x1;
+            f2_unpack(x, x0, x1);
+            float y0 = ex2_approx(x0), y1 = ex2_approx(x1);
+            if (!full) {
+              y0 = (key_ok && 2 * e < qvalid) ? y0 : 0.f;
+              y1 = (key_ok && 2 * e + 1 < qvalid) ? y1 : 0.f;
+            }
+            p2[e] = f2_pack(y0, y1);
+            pk[e] = F16 ? pack_f16x2(y0, y1) : pack_bf16x2(y0, y1);
+          }
         }
-        tmem_st16(st_t + qc * 16, pk);
+        tmem_st32(st_t + qh, pk);   // packed into this warpgroup's own (already read) columns
+        tmem_wait_st();
       }
-      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(p_ready);
 
       // dS^T = P^T (dP^T - delta), 32 queries at a time, into TMEM (dK MMA), smem (dQ MMA)
       // and the diagonal registers (dBias)
-      float dbin[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(dp_ready, i & 1, abort_flag, a.spin_limit))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float dbin[3] = {0.f, 0.f, 0.f};
 #pragma unroll
-      for (int qc = 0; qc < kBlk / 32; ++qc) {
+      for (int qc = 0; qc < kHalf / 32; ++qc) {
         uint32_t dsv[32];
-        tmem_ld32(dpt_t + qc * 32, dsv);
+        tmem_ld32(dpt_t + qh + qc * 32, dsv);
         tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int q = qc * 32 + e;
-          dsv[e] = __float_as_uint(p[q] * (__uint_as_float(dsv[e]) - del_p[q]));
-        }
         uint32_t dk[16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e)
-          dk[e] = F16 ? pack_f16x2(__uint_as_float(dsv[2 * e]), __uint_as_float(dsv[2 * e + 1]))
-                      : pack_bf16x2(__uint_as_float(dsv[2 * e]), __uint_as_float(dsv[2 * e + 1]));
-        tmem_st16(dpt_t + qc * 16, dk);
-        // smem copy for the dQ MMA: row kr of 64-query atom (qc/2), 16-byte chunks (qc%2)*4..+3
-        uint8_t* row = ds_smem + (qc / 2) * 16384 + kr * 128;
+        for (int j = 0; j < 8; ++j) {
+          const ulonglong2 nd = ndel2[qc * 8 + j];
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int e = 2 * j + t;     // pair within the chunk
+            const uint64_t d = f2_mul(p2[qc * 16 + e],
+                                      f2_add(f2_pack(__uint_as_float(dsv[2 * e]), __uint_as_float(dsv[2 * e + 1])),
+                                             t ? nd.y : nd.x));
+            float d0, d1;
+            f2_unpack(d, d0, d1);
+            dsv[2 * e] = __float_as_uint(d0);
+            dsv[2 * e + 1] = __float_as_uint(d1);
+            dk[e] = F16 ? pack_f16x2(d0, d1) : pack_bf16x2(d0, d1);
+          }
+        }
+        tmem_st16(dpt_t + qh + qc * 16, dk);
+        // smem copy for the dQ MMA: row kr of atom `half`, 16-byte chunks qc*4 .. qc*4+3
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int chunk = (qc % 2) * 4 + u;
-          *reinterpret_cast<uint4*>(row + ((chunk ^ (kr & 7)) << 4)) =
+          const int chunk = qc * 4 + u;
+          *reinterpret_cast<uint4*>(ds_row + ((chunk ^ (kr & 7)) << 4)) =
               make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
         }
         // diagonal transpose of this 32 x 32 sub-tile: m < 32 - lane stays on diagonal +lane
@@ -378,21 +457,22 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
       tc_fence_before();
       mbar_arrive(ds_ready);
       // this tile's diagonal sums: lane owns bins 31 - lane + 32 k
-      float* out = a.dbias_part + ((((size_t)bh * a.n_blk + kb) * a.n_blk + i) * 4 + quarter) * kBins;
+      float* out = a.dbias_part +
+                   ((((size_t)bh * a.n_blk + kb) * a.n_blk + i) * kWarpsPerTile + half * 4 + quarter) * kBins;
 #pragma unroll
-      for (int k = 0; k < 5; ++k) {
-        const int bin = 31 - lane + 32 * k;
-        if (bin < kBins) out[bin] = dbin[k];
-      }
+      for (int k = 0; k < 3; ++k) out[31 - lane + 32 * k] = dbin[k];
     }
     if (!ok) watchdog_fire(kWdBwdCompute);
   } else {
     regs_dec<kRegsDq>();
+    if constexpr (RES) fill_rows(threadIdx.x - 384 + 64);
     // ------------------------------------------------------------ dQ WG: one query row per thread
     const int quarter = warp % 4;
     const int r = quarter * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
     const uint32_t dq_t = tmem + lane_addr + C::kDQ;
+    const bool leader = threadIdx.x == 3 * 128;
+    float* stg_row = reinterpret_cast<float*>(smem + C::kStgOff) + (size_t)r * a.D;   // pitch D floats
     bool ok = true;
     for (int i = 0; i < nq; ++i) {
       if (!__all_sync(0xffffffffu, mbar_wait_bounded(dq_ready, i & 1, abort_flag, a.spin_limit))) {
@@ -400,23 +480,44 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
         break;
       }
       tc_fence_after();
-      float v[DP];
-      {
-        uint32_t* u = reinterpret_cast<uint32_t*>(v);
+      // the staging tile is free once the previous reduce-add has read it (mbarriers, not bar.sync,
+      // so that every wait stays bounded)
+      if (leader) {
+        bulk_wait_read_all();
+        mbar_arrive(stg_free);
+      }
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(stg_free, i & 1, abort_flag, a.spin_limit))) {
+        ok = false;
+        break;
+      }
 #pragma unroll
-        for (int c = 0; c < DP; c += 16) tmem_ld16(dq_t + c, u + c);
+      for (int c = 0; c < DP; c += 16) {
+        uint32_t u[16];
+        tmem_ld16(dq_t + c, u);
         tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; e += 4)
+          if (c + e < a.D)
+            *reinterpret_cast<uint4*>(stg_row + c + e) = make_uint4(u[e], u[e + 1], u[e + 2], u[e + 3]);
       }
       tc_fence_before();
       mbar_arrive(dq_free);
-      const int q = i * kBlk + r;
-      if (q < a.S) {
-        float* dst = a.dq_acc + ((size_t)b * a.S + q) * ((size_t)a.H * a.D) + (size_t)h * a.D;
-#pragma unroll
-        for (int c = 0; c < DP; c += 4)
-          if (c < a.D) red_add_v4(dst + c, v[c], v[c + 1], v[c + 2], v[c + 3]);
+      fence_async_shared();   // staging writes -> visible to the TMA unit
+      mbar_arrive(stg_full);
+      if (leader) {
+        if (!mbar_wait_bounded(stg_full, i & 1, abort_flag, a.spin_limit)) {
+          ok = false;
+        } else {
+          tma_reduce_add_3d(&dqmap, smem + C::kStgOff, h * a.D, i * kBlk, b);
+          bulk_commit_group();
+        }
+      }
+      if (!__all_sync(0xffffffffu, ok)) {   // the leader's failure ends its whole warp
+        ok = false;
+        break;
       }
     }
+    if (leader) bulk_wait_all();
     // dK, dV (rows = keys) -> dqkv
     if (ok && !__all_sync(0xffffffffu, mbar_wait_bounded(kdv_done, 0, abort_flag, a.spin_limit))) ok = false;
     if (!ok) {
@@ -520,9 +621,9 @@ relpos_bwd_dq_kernel(const float* __restrict__ dq_acc, void* __restrict__ dqkv, 
 }
 
 // dpd[h, t] = sum over b, over the tiles (kb, qb) whose diagonal range covers g = t - (S-1) =
-// key - query, and over the four key-quarter warps of each tile, of the bin holding g.  A tile at
-// offset d = kb - qb holds diagonal e = g - 128 d of quarter w in bin 31 - e + 32 w.  Fixed order:
-// deterministic.
+// key - query, and over the eight (query half, key quarter) warps of each tile, of the bin holding
+// g.  A tile at offset d = kb - qb holds tile diagonal e = g - 128 d; warp (half, quarter) holds it
+// in bin 32 quarter - 64 half + 31 - e.  Fixed order: deterministic.
 __global__ void __launch_bounds__(256)
 relpos_bwd_dpd_kernel(const float* __restrict__ part, float* __restrict__ dpd, int B, int S, int H, int nb) {
   const int h = blockIdx.y;
@@ -532,17 +633,17 @@ relpos_bwd_dpd_kernel(const float* __restrict__ part, float* __restrict__ dpd, i
   const int d_hi = (g + 127) >= 0 ? (g + 127) / 128 : -((-(g + 127) + 127) / 128);
   float acc = 0.f;
   for (int bb = 0; bb < B; ++bb) {
-    const float* pb = part + (size_t)(bb * H + h) * nb * nb * 4 * kBins;
+    const float* pb = part + (size_t)(bb * H + h) * nb * nb * kWarpsPerTile * kBins;
     for (int d = d_hi; d >= d_hi - 1; --d) {
       const int e = g - 128 * d;
       if (e < -(kBlk - 1) || e > kBlk - 1) continue;
       const int kb_lo = d > 0 ? d : 0, kb_hi = d > 0 ? nb : nb + d;   // qb = kb - d in [0, nb)
       for (int kbi = kb_lo; kbi < kb_hi; ++kbi) {
-        const float* tile = pb + ((size_t)kbi * nb + (kbi - d)) * 4 * kBins;
+        const float* tile = pb + ((size_t)kbi * nb + (kbi - d)) * kWarpsPerTile * kBins;
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          const int j = 31 - e + 32 * w;
-          if (j >= 0 && j < kBlk + 31) acc += tile[w * kBins + j];
+        for (int w = 0; w < kWarpsPerTile; ++w) {
+          const int j = 32 * (w % 4) - 64 * (w / 4) + 31 - e;
+          if (j >= 0 && j < kBins) acc += tile[w * kBins + j];
         }
       }
     }
@@ -561,12 +662,12 @@ inline WsLayout ws_layout(int64_t B, int64_t S, int64_t H, int64_t D) {
   w.delta = 0;
   w.dq = up((size_t)B * H * S * 4);
   w.part = w.dq + up((size_t)B * S * H * D * 4);
-  w.total = w.part + up((size_t)B * H * nb * nb * 4 * kBins * 4);
+  w.total = w.part + up((size_t)B * H * nb * nb * kWarpsPerTile * kBins * 4);
   return w;
 }
 
 template <int DP, bool F16>
-int launch_bwd(const CUtensorMap& qm, const CUtensorMap& om, const BwdArgs& a, const void* dout,
+int launch_bwd(const CUtensorMap& qm, const CUtensorMap& om, const CUtensorMap& dqm, const BwdArgs& a, const void* dout,
                const float* out32, float* dpd, cudaStream_t stream) {
   using C = BwdCfg<DP>;
   const int64_t tokens_heads = (int64_t)a.B * a.S * a.H;
@@ -578,7 +679,7 @@ int launch_bwd(const CUtensorMap& qm, const CUtensorMap& om, const BwdArgs& a, c
   auto kern = res ? relpos_bwd_main_kernel<DP, F16, true> : relpos_bwd_main_kernel<DP, F16, false>;
   const size_t smem = res ? res_smem : C::kSmem;
   KRSI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  kern<<<dim3(a.n_blk, a.B * a.H), kThreads, smem, stream>>>(qm, om, a);
+  kern<<<dim3(a.n_blk, a.B * a.H), kThreads, smem, stream>>>(qm, om, dqm, a);
   KRSI_LAUNCH_CHECK();
   const int64_t rows = (int64_t)a.B * a.S;
   const int64_t items = rows * (a.H * a.D / 8);
@@ -592,12 +693,12 @@ int launch_bwd(const CUtensorMap& qm, const CUtensorMap& om, const BwdArgs& a, c
 }
 
 template <bool F16>
-int dispatch_dp(int DP, const CUtensorMap& qm, const CUtensorMap& om, const BwdArgs& a, const void* dout,
-                const float* out32, float* dpd, cudaStream_t s) {
+int dispatch_dp(int DP, const CUtensorMap& qm, const CUtensorMap& om, const CUtensorMap& dqm, const BwdArgs& a,
+                const void* dout, const float* out32, float* dpd, cudaStream_t s) {
   switch (DP) {
-    case 32: return launch_bwd<32, F16>(qm, om, a, dout, out32, dpd, s);
-    case 64: return launch_bwd<64, F16>(qm, om, a, dout, out32, dpd, s);
-    case 80: return launch_bwd<80, F16>(qm, om, a, dout, out32, dpd, s);
+    case 32: return launch_bwd<32, F16>(qm, om, dqm, a, dout, out32, dpd, s);
+    case 64: return launch_bwd<64, F16>(qm, om, dqm, a, dout, out32, dpd, s);
+    case 80: return launch_bwd<80, F16>(qm, om, dqm, a, dout, out32, dpd, s);
     default: return KRSI_ERR_UNSUPPORTED;
   }
 }
@@ -636,10 +737,11 @@ extern "C" int krsi_relpos_attn_bwd(const void* dout, const void* qkv, int64_t q
   const WsLayout ws = ws_layout(B, S, H, D);
   if (!workspace || workspace_bytes < ws.total || !aligned16(workspace)) return KRSI_ERR_WORKSPACE;
   uint8_t* w = static_cast<uint8_t*>(workspace);
-  CUtensorMap qm, om;
+  CUtensorMap qm, om, dqm;
   const bool f16 = dtype == KRSI_F16;
   if (!attn::make_head_map(&qm, qkv, qkv_row_stride, B, S, 3 * H, D, f16) ||
-      !attn::make_head_map(&om, dout, H * D, B, S, H, D, f16))
+      !attn::make_head_map(&om, dout, H * D, B, S, H, D, f16) ||
+      !attn::make_rows_f32_map(&dqm, reinterpret_cast<float*>(w + ws.dq), B, S, H, D))
     return KRSI_ERR_CUDA;
   BwdArgs a{pd,
             lse,
@@ -656,6 +758,6 @@ extern "C" int krsi_relpos_attn_bwd(const void* dout, const void* qkv, int64_t q
             scale * 1.4426950408889634f,
             scale,
             kSpinLimit};
-  return f16 ? dispatch_dp<true>(DP, qm, om, a, dout, out32, dpd, stream)
-             : dispatch_dp<false>(DP, qm, om, a, dout, out32, dpd, stream);
+  return f16 ? dispatch_dp<true>(DP, qm, om, dqm, a, dout, out32, dpd, stream)
+             : dispatch_dp<false>(DP, qm, om, dqm, a, dout, out32, dpd, stream);
 }

@@ -79,7 +79,9 @@ def _worker(rank, world, port, q, mode):
             raise RuntimeError("planted failure on rank 1 before its first collective")
         x = shard_batch(global_batch(cfg), rank, world)
         loss = train_step(model, x, reducer, world, loss_fn)
-        grads = {n: p.grad.clone() for n, p in model.named_parameters()}
+        # numpy copies travel by value: a tensor would be shared through a file descriptor that
+        # dies with this process if it exits before the parent has received it
+        grads = {n: p.grad.detach().numpy().copy() for n, p in model.named_parameters()}
         q.put((rank, "ok", float(loss), grads))
     except Exception as e:  # noqa: BLE001
         q.put((rank, "error", f"{type(e).__name__}: {e}", None))
@@ -119,7 +121,7 @@ def test_two_rank_gradients_equal_full_batch():
     assert abs(res[0][1] + res[1][1] - float(loss)) < 1e-5 * max(1.0, abs(float(loss)))
     for r in (0, 1):
         for n, g in res[r][2].items():
-            torch.testing.assert_close(g, ref[n], rtol=1e-4, atol=1e-6)
+            torch.testing.assert_close(torch.from_numpy(g), ref[n], rtol=1e-4, atol=1e-6)
 
 
 def test_dead_rank_raises_instead_of_hanging():
