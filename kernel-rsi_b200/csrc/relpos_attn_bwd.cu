@@ -210,7 +210,30 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
     const float* pdh = a.pd + (size_t)h * two_s;
     const float* lse_bh = a.lse + (size_t)bh * a.S;
     const float* del_bh = a.delta + (size_t)bh * a.S;
-
+    // A block's per-query vectors are fetched into registers one block ahead, so filling a stage
+    // never waits on global memory: -lse and -delta (zero past S) and, when the bias row is not
+    // resident, slab[t] = pd[h, k0 - q0 + 127 - t + S - 1] * log2e for t in [0, 255) (so that
+    // bias(k0 + kr, q0 + q) = slab[127 - kr + q]) with its copy slab1[t] = slab[t + 1].
+    float nl[4], nd[4], sl0[8], sl1[8];
+    auto fetch = [&](int blk) {
+      const int q0 = blk * kBlk;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int q = q0 + lane + 32 * k;
+        nl[k] = q < a.S ? -__ldg(lse_bh + q) : 0.f;
+        nd[k] = q < a.S ? -__ldg(del_bh + q) : 0.f;
+      }
+      if constexpr (!RES) {
+        const int top = k0 - q0 + kBlk - 1 + a.S - 1;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int tt = lane + 32 * k, pos = top - tt;
+          sl0[k] = (tt < 2 * kBlk - 1 && pos >= 0 && pos < two_s) ? __ldg(pdh + pos) * kLog2e : 0.f;
+          sl1[k] = (tt + 1 < 2 * kBlk - 1 && pos - 1 >= 0 && pos - 1 < two_s) ? __ldg(pdh + pos - 1) * kLog2e : 0.f;
+        }
+      }
+    };
+    fetch(0);
     for (int i = 0; i < nq; ++i) {
       const int s = i % NQS;
       if (i >= NQS && !mbar_wait_bounded(&qdo_empty[s], ((i / NQS) + 1) & 1, abort_flag, a.spin_limit)) {
@@ -225,23 +248,21 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
         attn::load_tile<DP>(qt + C::kTile, &omap, &qdo_full[s], h, q0, b);
       }
       float* vec = reinterpret_cast<float*>(smem + C::kVecOff + s * C::kVecBytes);
-      for (int r = lane; r < kBlk; r += 32) {
-        const int q = q0 + r;
-        vec[r] = q < a.S ? -__ldg(lse_bh + q) : 0.f;
-        vec[128 + r] = q < a.S ? -__ldg(del_bh + q) : 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        vec[lane + 32 * k] = nl[k];
+        vec[128 + lane + 32 * k] = nd[k];
       }
       if constexpr (!RES) {
-      // slab[t] = pd[h, k0 - q0 + 127 - t + S - 1] * log2e for t in [0, 255), so that
-      // bias(k0 + kr, q0 + q) = slab[127 - kr + q]; slab1[t] = slab[t + 1]
-      const int top = k0 - q0 + kBlk - 1 + a.S - 1;
-      for (int t = lane; t < 256; t += 32) {
-        const int pos = top - t;
-        vec[256 + t] = (t < 2 * kBlk - 1 && pos >= 0 && pos < two_s) ? __ldg(pdh + pos) * kLog2e : 0.f;
-        vec[512 + t] = (t + 1 < 2 * kBlk - 1 && pos - 1 >= 0 && pos - 1 < two_s) ? __ldg(pdh + pos - 1) * kLog2e : 0.f;
-      }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          vec[256 + lane + 32 * k] = sl0[k];
+          vec[512 + lane + 32 * k] = sl1[k];
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&qdo_full[s]);
+      if (i + 1 < nq) fetch(i + 1);
     }
   } else if (warp == 2 || warp == 3) {
     if constexpr (RES) fill_rows(threadIdx.x - 64);
@@ -370,36 +391,44 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
       const bool full = keys_full && q0 + kBlk <= a.S;
       const int qvalid = a.S - q0 - qh;        // queries of this warpgroup inside the sequence
 
-      // P^T = exp2(s2 - lse) in paired fp32; 16-bit copy over S^T in TMEM
+      // P^T = exp2(s2 - lse) in paired fp32, 32 queries at a time (bounded register use); three
+      // of every four pairs on the SFU, one on the FMA pipe; 16-bit copy over S^T in TMEM
       uint64_t p2[kHalf / 2];
-      {
-        uint32_t u[kHalf];
-        tmem_ld32(st_t + qh, u);
-        tmem_ld32(st_t + qh + 32, u + 32);
+#pragma unroll
+      for (int qc = 0; qc < kHalf / 32; ++qc) {
+        uint32_t u[32];
+        tmem_ld32(st_t + qh + qc * 32, u);
         tmem_wait_ld();
-        uint32_t pk[kHalf / 2];
+        uint32_t pk[16];
 #pragma unroll
-        for (int j = 0; j < kHalf / 4; ++j) {
-          const ulonglong2 nl = nlse2[j];
+        for (int j = 0; j < 8; ++j) {
+          const ulonglong2 nl = nlse2[qc * 8 + j];
 #pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const int e = 2 * j + t;   // pair index: queries 2e, 2e + 1
-            uint64_t x = f2_fma(f2_pack(__uint_as_float(u[2 * e]), __uint_as_float(u[2 * e + 1])), scale2, bq2[e]);
-            x = f2_add(x, t ? nl.y : nl.x);
-            float x0, x1;
+          for (int tq = 0; tq < 2; ++tq) {
+            const int e = 2 * j + tq;      // pair within the chunk: queries 2e, 2e + 1
+            const int pe = qc * 16 + e;    // pair within this warpgroup's 64 queries
+            uint64_t x = f2_fma(f2_pack(__uint_as_float(u[2 * e]), __uint_as_float(u[2 * e + 1])), scale2, bq2[pe]);
+            x = f2_add(x, tq ? nl.y : nl.x);
+            float x0, x1, y0, y1;
             f2_unpack(x, x0, x1);
-            float y0 = ex2_approx(x0), y1 = ex2_approx(x1);
-            if (!full) {
-              y0 = (key_ok && 2 * e < qvalid) ? y0 : 0.f;
-              y1 = (key_ok && 2 * e + 1 < qvalid) ? y1 : 0.f;
+            if (e % 4 == 3) {
+              exp2_poly3_x2(x0, x1, y0, y1);
+            } else {
+              y0 = ex2_approx(x0);
+              y1 = ex2_approx(x1);
             }
-            p2[e] = f2_pack(y0, y1);
+            if (!full) {
+              y0 = (key_ok && 2 * pe < qvalid) ? y0 : 0.f;
+              y1 = (key_ok && 2 * pe + 1 < qvalid) ? y1 : 0.f;
+            }
+            p2[pe] = f2_pack(y0, y1);
             pk[e] = F16 ? pack_f16x2(y0, y1) : pack_bf16x2(y0, y1);
           }
         }
-        tmem_st32(st_t + qh, pk);   // packed into this warpgroup's own (already read) columns
-        tmem_wait_st();
+        // packed into this warpgroup's own columns, which it has already read
+        tmem_st16(st_t + qh + qc * 16, pk);
       }
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(p_ready);
 
