@@ -59,6 +59,7 @@ constexpr uint32_t kRegsDq = 88;
 constexpr int kWarpsPerTile = 8;    // dBias partial rows per tile: (query half, key quarter)
 constexpr int kBins = 96;           // per-warp bins: 32 keys x 64 queries -> 95 diagonals (+1 zero)
 constexpr int kRowFillers = 192;    // warps 2-3 and 12-15 fill the resident rows
+constexpr int kCopyBank = 16;       // distance (mod 32 floats) between the two bias copies
 
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -72,9 +73,10 @@ struct BwdCfg {
   static constexpr uint32_t kDSOff = kQOff + NQS * 2 * kTile;     // dS (bf16, MN-major SW128): 2 x 16 KB
   static constexpr uint32_t kStgOff = kDSOff + 2 * 16384;          // dQ tile staging: 128 rows x D fp32
   // per stage: -lse[128], -delta[128] and (bias not resident) the reversed bias slab [256] with its
-  // copy shifted by one element [256]
+  // copy shifted by one element [256] placed kCopyBank (mod 32) floats after it (bank-conflict-free)
   static constexpr uint32_t kVecOff = kStgOff + kTileRows * DP * 4;
-  static constexpr uint32_t kVecBytes = (128 + 128 + 2 * 256) * 4;
+  static constexpr int kSlab0 = 256, kSlab1 = 256 + 256 + kCopyBank;
+  static constexpr uint32_t kVecBytes = (kSlab1 + 256) * 4;
   static constexpr uint32_t kBarOff = kVecOff + NQS * kVecBytes;
   static constexpr int kNumBars = 1 + 2 * NQS + 11;
   static constexpr uint32_t kMiscOff = kBarOff + kNumBars * 8;
@@ -109,9 +111,13 @@ __host__ __device__ constexpr uint32_t packed_col(int kk) { return kk * 8 + (kk 
 //   rev[kRevPad + t] = pd[h, m_top - t] * log2e   (zero outside [0, 2S-2]),
 // so bias(k0 + kr, q) = rev[kRevPad + 127 - kr + q] ascends with the query, and a second copy
 // shifted by one element (rev1[i] = rev[i + 1]) makes every pair of queries an aligned 8-byte read.
+// A thread's first pair starts at kRevPad + 127 - key_row + (even), an odd index for kRevPad = 4, so
+// in a half-warp the lanes on copy 0 read 16 consecutive floats and the lanes on copy 1 the 16 floats
+// just after them, shifted by the copy distance minus 16.  With the copies 16 (mod 32) floats apart
+// the two halves fall on disjoint banks: one wavefront per half-warp.
 constexpr int kRevPad = 4;
 __host__ __device__ constexpr int64_t rev_row_floats(int64_t S) {
-  return ((kRevPad + ((S + kBlk - 1) / kBlk) * kBlk + kBlk + 4) + 3) & ~int64_t(3);
+  return (kRevPad + ((S + kBlk - 1) / kBlk) * kBlk + kBlk + 4 + 31 - kCopyBank) / 32 * 32 + kCopyBank;
 }
 __host__ __device__ constexpr int64_t rows_bytes(int64_t S) { return 2 * rev_row_floats(S) * 4; }
 
@@ -256,8 +262,8 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
       if constexpr (!RES) {
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          vec[256 + lane + 32 * k] = sl0[k];
-          vec[512 + lane + 32 * k] = sl1[k];
+          vec[C::kSlab0 + lane + 32 * k] = sl0[k];
+          vec[C::kSlab1 + lane + 32 * k] = sl1[k];
         }
       }
       __syncwarp();
@@ -385,8 +391,8 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
       const ulonglong2* ndel2 = reinterpret_cast<const ulonglong2*>(vec + 128 + qh);
       // bias(key, q0 + qh + q) = bq[q], read as aligned pairs from whichever copy makes them aligned
       const int bbase = RES ? kRevPad + kBlk - 1 - kr + q0 + qh : kBlk - 1 - kr + qh;
-      const float* c0 = RES ? rev0 : vec + 256;
-      const float* c1 = RES ? rev1 : vec + 512;
+      const float* c0 = RES ? rev0 : vec + C::kSlab0;
+      const float* c1 = RES ? rev1 : vec + C::kSlab1;
       const uint64_t* bq2 = reinterpret_cast<const uint64_t*>((bbase & 1) ? c1 + bbase - 1 : c0 + bbase);
       const bool full = keys_full && q0 + kBlk <= a.S;
       const int qvalid = a.S - q0 - qh;        // queries of this warpgroup inside the sequence

@@ -56,7 +56,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
                                                   uint32_t limit) {
   for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
+    if ((i & 15u) == 15u && *abort_flag) return false;   // polled sparingly: shared-memory traffic
   }
   *abort_flag = 1;
   return false;
