@@ -11,7 +11,11 @@
 //   bwd_main   one CTA per (b*H + h, 128-key block); loops over the 128-query blocks with four
 //              warpgroups:
 //                warp 0      TMA producer: K and V once; Q and dO tiles per query block (2 stages)
-//                            and the block's -lse, -delta (and bias slab when not resident)
+//                            and the block's -lse, -delta (and bias slab when not resident).  When
+//                            D leaves padding columns (D % 16 == 8) it writes K, V = 1 and Q, dO =
+//                            a three-term 16-bit split of -lse / (scale log2 e) and -delta into
+//                            padding columns D..D+2, so the S^T and dP^T MMAs produce S - lse/c
+//                            and dP - delta directly (no per-element lse/delta reads)
 //                warp 1      TMEM owner + tcgen05.mma issuer, software-pipelined so the next
 //                            block's S^T is computed while the current dS is:
 //                              S^T = K Q^T, dP^T = V dO^T              (SS, K = DP)
@@ -78,7 +82,7 @@ struct BwdCfg {
   static constexpr int kSlab0 = 256, kSlab1 = 256 + 256 + kCopyBank;
   static constexpr uint32_t kVecBytes = (kSlab1 + 256) * 4;
   static constexpr uint32_t kBarOff = kVecOff + NQS * kVecBytes;
-  static constexpr int kNumBars = 1 + 2 * NQS + 11;
+  static constexpr int kNumBars = 1 + 3 * NQS + 11;
   static constexpr uint32_t kMiscOff = kBarOff + kNumBars * 8;
   static constexpr uint32_t kRowOff = (kMiscOff + 16 + 15) & ~15u;   // resident rows (runtime length)
   static constexpr uint32_t kSmem = kRowOff + 1024;                  // + the 1 KB alignment slack
@@ -121,7 +125,21 @@ __host__ __device__ constexpr int64_t rev_row_floats(int64_t S) {
 }
 __host__ __device__ constexpr int64_t rows_bytes(int64_t S) { return 2 * rev_row_floats(S) * 4; }
 
-template <int DP, bool F16, bool RES>
+// 16-byte chunk of padding columns [D, D + 8) of row r of a tile (D % 16 == 8: the second chunk of
+// 32-byte block D / 16; the 32-byte swizzle flips the chunk on every fourth row).
+__device__ __forceinline__ uint4* pad_chunk(uint8_t* tile, int D, int r) {
+  return reinterpret_cast<uint4*>(tile + (D / 16) * attn::kBlockBytes + r * 32 + ((1 ^ ((r >> 2) & 1)) << 4));
+}
+// v as hi + mid + lo, each rounded to the 16-bit input type, in the first three columns of a chunk
+template <bool F16>
+__device__ __forceinline__ uint4 split3(float v) {
+  auto rnd = [](float x) { return F16 ? __half2float(__float2half_rn(x)) : __bfloat162float(__float2bfloat16_rn(x)); };
+  const float hi = rnd(v), r1 = v - hi, mid = rnd(r1), lo = rnd(r1 - mid);
+  return F16 ? make_uint4(pack_f16x2(hi, mid), pack_f16x2(lo, 0.f), 0u, 0u)
+             : make_uint4(pack_bf16x2(hi, mid), pack_bf16x2(lo, 0.f), 0u, 0u);
+}
+
+template <int DP, bool F16, bool RES, bool FOLD>
 __global__ void __launch_bounds__(kThreads, 1)
 relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap omap,
                        const __grid_constant__ CUtensorMap dqmap, const BwdArgs a) {
@@ -133,7 +151,8 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
   uint64_t* kv_full = bars;
   uint64_t* qdo_full = bars + 1;
   uint64_t* qdo_empty = bars + 1 + NQS;
-  uint64_t* s_ready = bars + 1 + 2 * NQS;   // S^T of the current block in TMEM
+  uint64_t* qdo_tma = bars + 1 + 2 * NQS;   // the stage's TMA loads have landed (producer waits)
+  uint64_t* s_ready = bars + 1 + 3 * NQS;   // S^T of the current block in TMEM
   uint64_t* dp_ready = s_ready + 1;          // dP^T of the current block in TMEM
   uint64_t* p_ready = s_ready + 2;           // P^T written (256 compute threads)
   uint64_t* ds_ready = s_ready + 3;          // dS^T written to TMEM and smem (256)
@@ -157,7 +176,8 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
     for (int s = 0; s < NQS; ++s) {
-      mbar_init(&qdo_full[s], 2);   // TMA expect_tx + the producer's vectors
+      mbar_init(&qdo_full[s], 1);   // the producer, after the TMA landed and its own writes
+      mbar_init(&qdo_tma[s], 1);
       mbar_init(&qdo_empty[s], 1);
     }
     mbar_init(s_ready, 1);
@@ -206,18 +226,39 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
   if (warp < 4) {
     regs_dec<kRegsCtl>();
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------------------ TMA producer
+    // Loads K, V once, then each block's Q and dO as soon as its stage is released (no other work,
+    // so a released stage is refilled at once).
     if (lane == 0) {
       mbar_arrive_expect_tx(kv_full, 2 * C::kTile);
       attn::load_tile<DP>(smem + C::kKOff, &qmap, kv_full, a.H + h, k0, b);
       attn::load_tile<DP>(smem + C::kVOff, &qmap, kv_full, 2 * a.H + h, k0, b);
+      for (int i = 0; i < nq; ++i) {
+        const int s = i % NQS;
+        if (i >= NQS && !mbar_wait_bounded(&qdo_empty[s], ((i / NQS) + 1) & 1, abort_flag, a.spin_limit)) {
+          watchdog_fire(kWdBwdLoad);
+          break;
+        }
+        uint8_t* qt = smem + C::kQOff + s * 2 * C::kTile;
+        mbar_arrive_expect_tx(&qdo_tma[s], 2 * C::kTile);
+        attn::load_tile<DP>(qt, &qmap, &qdo_tma[s], h, i * kBlk, b);
+        attn::load_tile<DP>(qt + C::kTile, &omap, &qdo_tma[s], h, i * kBlk, b);
+      }
     }
+  } else if (warp == 2) {
+    if constexpr (RES) fill_rows(threadIdx.x - 64);
+  } else if (warp == 3) {
+    if constexpr (RES) fill_rows(threadIdx.x - 64);
+    // ------------------------------------------------------------ stage finisher
+    // Publishes each stage once its TMA loads have landed, after writing the block's per-query
+    // vectors (unfolded) or the padding columns (folded) and, when the bias row is not resident,
+    // the block's bias slab.
     const int two_s = 2 * a.S - 1;
     const float* pdh = a.pd + (size_t)h * two_s;
     const float* lse_bh = a.lse + (size_t)bh * a.S;
     const float* del_bh = a.delta + (size_t)bh * a.S;
-    // A block's per-query vectors are fetched into registers one block ahead, so filling a stage
-    // never waits on global memory: -lse and -delta (zero past S) and, when the bias row is not
+    // A block's vectors are fetched into registers one block ahead, so filling a stage never
+    // waits on global memory: -lse and -delta (zero past S) and, when the bias row is not
     // resident, slab[t] = pd[h, k0 - q0 + 127 - t + S - 1] * log2e for t in [0, 255) (so that
     // bias(k0 + kr, q0 + q) = slab[127 - kr + q]) with its copy slab1[t] = slab[t + 1].
     float nl[4], nd[4], sl0[8], sl1[8];
@@ -239,25 +280,25 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
         }
       }
     };
+    const float inv_c = 1.f / a.scale_log2;   // Q padding carries -lse / (scale log2 e)
     fetch(0);
     for (int i = 0; i < nq; ++i) {
       const int s = i % NQS;
-      if (i >= NQS && !mbar_wait_bounded(&qdo_empty[s], ((i / NQS) + 1) & 1, abort_flag, a.spin_limit)) {
+      uint8_t* qt = smem + C::kQOff + s * 2 * C::kTile;
+      float* vec = reinterpret_cast<float*>(smem + C::kVecOff + s * C::kVecBytes);
+      // the vectors and slab live outside the TMA tiles and the stage is free (its previous
+      // block's readers finished before the producer reloaded it): write them before the wait
+      if (!__all_sync(0xffffffffu, i < NQS || mbar_wait_bounded(&qdo_empty[s], ((i / NQS) + 1) & 1, abort_flag,
+                                                                 a.spin_limit))) {
         watchdog_fire(kWdBwdLoad);
         break;
       }
-      const int q0 = i * kBlk;
-      uint8_t* qt = smem + C::kQOff + s * 2 * C::kTile;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&qdo_full[s], 2 * C::kTile);
-        attn::load_tile<DP>(qt, &qmap, &qdo_full[s], h, q0, b);
-        attn::load_tile<DP>(qt + C::kTile, &omap, &qdo_full[s], h, q0, b);
-      }
-      float* vec = reinterpret_cast<float*>(smem + C::kVecOff + s * C::kVecBytes);
+      if constexpr (!FOLD) {
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        vec[lane + 32 * k] = nl[k];
-        vec[128 + lane + 32 * k] = nd[k];
+        for (int k = 0; k < 4; ++k) {
+          vec[lane + 32 * k] = nl[k];
+          vec[128 + lane + 32 * k] = nd[k];
+        }
       }
       if constexpr (!RES) {
 #pragma unroll
@@ -266,12 +307,37 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
           vec[C::kSlab1 + lane + 32 * k] = sl1[k];
         }
       }
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&qdo_tma[s], (i / NQS) & 1, abort_flag, a.spin_limit))) {
+        watchdog_fire(kWdBwdLoad);
+        break;
+      }
+      if constexpr (FOLD) {
+        if (i == 0) {   // K and V: ones in the three padding columns (once; they stay resident)
+          if (!__all_sync(0xffffffffu, mbar_wait_bounded(kv_full, 0, abort_flag, a.spin_limit))) {
+            watchdog_fire(kWdBwdLoad);
+            break;
+          }
+          const uint32_t one2 = F16 ? pack_f16x2(1.f, 1.f) : pack_bf16x2(1.f, 1.f);
+          const uint32_t one1 = F16 ? pack_f16x2(1.f, 0.f) : pack_bf16x2(1.f, 0.f);
+          const uint4 one3 = make_uint4(one2, one1, 0u, 0u);   // 1 in columns D, D+1, D+2
+          for (int r = lane; r < kBlk; r += 32) {
+            *pad_chunk(smem + C::kKOff, a.D, r) = one3;
+            *pad_chunk(smem + C::kVOff, a.D, r) = one3;
+          }
+        }
+        // over the TMA's zero fill of the padding columns
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int r = lane + 32 * k;
+          *pad_chunk(qt, a.D, r) = split3<F16>(nl[k] * inv_c);
+          *pad_chunk(qt + C::kTile, a.D, r) = split3<F16>(nd[k]);
+        }
+        fence_async_shared();   // generic writes to MMA operands -> visible to the async proxy
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&qdo_full[s]);
       if (i + 1 < nq) fetch(i + 1);
     }
-  } else if (warp == 2 || warp == 3) {
-    if constexpr (RES) fill_rows(threadIdx.x - 64);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -337,13 +403,13 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
 #pragma unroll
         for (int kk = 0; kk < kBlk / 16; ++kk)
           mma_ts(tmem + C::kDK, tmem + C::kDPT + packed_col(kk), q_mn0 + so + kk * attn::kKRowStep, id_nd, kk > 0 ? 1u : acc0);
+        mma_commit(&qdo_empty[s]);   // Q and dO of this block are no longer read (dQ uses dS and K)
         if (i > 0 && !mbar_wait_bounded(dq_free, (i - 1) & 1, abort_flag, a.spin_limit)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kBlk / 16; ++kk)
           mma_ss(tmem + C::kDQ, ds_d + kk * kDsRows, k_mn + kk * attn::kKRowStep, id_dq, kk > 0 ? 1u : 0u);
         mma_commit(dq_ready);
-        mma_commit(&qdo_empty[s]);
         if (next) {
           issue_dp(s1);
           mma_commit(dp_ready);
@@ -408,13 +474,13 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
         uint32_t pk[16];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const ulonglong2 nl = nlse2[qc * 8 + j];
+          const ulonglong2 nl = FOLD ? ulonglong2{} : nlse2[qc * 8 + j];
 #pragma unroll
           for (int tq = 0; tq < 2; ++tq) {
             const int e = 2 * j + tq;      // pair within the chunk: queries 2e, 2e + 1
             const int pe = qc * 16 + e;    // pair within this warpgroup's 64 queries
             uint64_t x = f2_fma(f2_pack(__uint_as_float(u[2 * e]), __uint_as_float(u[2 * e + 1])), scale2, bq2[pe]);
-            x = f2_add(x, tq ? nl.y : nl.x);
+            if constexpr (!FOLD) x = f2_add(x, tq ? nl.y : nl.x);
             float x0, x1, y0, y1;
             f2_unpack(x, x0, x1);
             if (e % 4 == 3) {
@@ -454,13 +520,12 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
         uint32_t dk[16];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const ulonglong2 nd = ndel2[qc * 8 + j];
+          const ulonglong2 nd = FOLD ? ulonglong2{} : ndel2[qc * 8 + j];
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
             const int e = 2 * j + t;     // pair within the chunk
-            const uint64_t d = f2_mul(p2[qc * 16 + e],
-                                      f2_add(f2_pack(__uint_as_float(dsv[2 * e]), __uint_as_float(dsv[2 * e + 1])),
-                                             t ? nd.y : nd.x));
+            const uint64_t dp = f2_pack(__uint_as_float(dsv[2 * e]), __uint_as_float(dsv[2 * e + 1]));
+            const uint64_t d = f2_mul(p2[qc * 16 + e], FOLD ? dp : f2_add(dp, t ? nd.y : nd.x));
             float d0, d1;
             f2_unpack(d, d0, d1);
             dsv[2 * e] = __float_as_uint(d0);
@@ -711,7 +776,9 @@ int launch_bwd(const CUtensorMap& qm, const CUtensorMap& om, const CUtensorMap& 
   KRSI_LAUNCH_CHECK();
   const size_t res_smem = C::kSmem + (size_t)rows_bytes(a.S);
   const bool res = res_smem <= 232448;   // 227 KB per CTA on sm_100
-  auto kern = res ? relpos_bwd_main_kernel<DP, F16, true> : relpos_bwd_main_kernel<DP, F16, false>;
+  const bool fold = a.D % 16 == 8;       // padding columns D..D+2 free for -lse / -delta
+  auto kern = res ? (fold ? relpos_bwd_main_kernel<DP, F16, true, true> : relpos_bwd_main_kernel<DP, F16, true, false>)
+                  : (fold ? relpos_bwd_main_kernel<DP, F16, false, true> : relpos_bwd_main_kernel<DP, F16, false, false>);
   const size_t smem = res ? res_smem : C::kSmem;
   KRSI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   kern<<<dim3(a.n_blk, a.B * a.H), kThreads, smem, stream>>>(qm, om, dqm, a);

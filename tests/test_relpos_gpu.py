@@ -130,9 +130,18 @@ def attn_bwd_check(B, S, H, D, dtype=torch.bfloat16, seed=0, tol=1e-2):
     (1, 17, 2, 72),
     (1, 1, 1, 72),
     (1, 520, 2, 32),
+    (1, 300, 2, 56),     # D % 16 == 8 with 64 padded columns: -lse / -delta folded into the MMAs
+    (1, 200, 1, 24),
 ])
 def test_bwd_small_shapes(B, S, H, D):
     attn_bwd_check(B, S, H, D, seed=7 * S + D)
+
+
+@pytest.mark.parametrize("D", [72, 64])
+def test_bwd_streamed_bias(D):
+    """S = 4608: the reversed bias window no longer fits beside the tiles, so each query block's bias
+    slab is streamed with its Q/dO stage (folded and unfolded lse/delta)."""
+    attn_bwd_check(1, 4608, 1, D, seed=D)
 
 
 def test_bwd_f16():
