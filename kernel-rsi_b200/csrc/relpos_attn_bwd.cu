@@ -340,7 +340,11 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the issue loop (warp-uniform descriptors); one elected lane issues.
+    {
+      auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, abort_flag, a.spin_limit));
+      };
       constexpr uint32_t fmt = F16 ? 0u : 1u;
       constexpr uint32_t id_sq = idesc_f16(128, kBlk, fmt, false, false);   // S^T, dP^T: K-major, N = 128
       constexpr uint32_t id_nd = idesc_f16(128, DP, fmt, false, true);      // dV, dK: B MN-major, N = DP
@@ -360,25 +364,25 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
       auto issue_s = [&](int s) {        // S^T = K Q^T (rows = keys)
 #pragma unroll
         for (int kk = 0; kk < DP / 16; ++kk)
-          mma_ss(tmem + C::kST, k_kd + kk * attn::kKSliceStep, q_kd0 + s * kStage + kk * attn::kKSliceStep, id_sq,
+          mma_ss_e(tmem + C::kST, k_kd + kk * attn::kKSliceStep, q_kd0 + s * kStage + kk * attn::kKSliceStep, id_sq,
                  kk > 0);
       };
       auto issue_dp = [&](int s) {       // dP^T = V dO^T
 #pragma unroll
         for (int kk = 0; kk < DP / 16; ++kk)
-          mma_ss(tmem + C::kDPT, v_kd + kk * attn::kKSliceStep, o_kd0 + s * kStage + kk * attn::kKSliceStep, id_sq,
+          mma_ss_e(tmem + C::kDPT, v_kd + kk * attn::kKSliceStep, o_kd0 + s * kStage + kk * attn::kKSliceStep, id_sq,
                  kk > 0);
       };
       // Order per block i (in-order tensor pipe, so every overwrite follows the reads before it):
       //   [P_i] dV_i, S_{i+1} -> s_ready   [dS_i] dK_i, dQ_i, dP_{i+1} -> dp_ready
-      bool ok = mbar_wait_bounded(kv_full, 0, abort_flag, a.spin_limit) &&
-                mbar_wait_bounded(&qdo_full[0], 0, abort_flag, a.spin_limit);
+      bool ok = wait_all(kv_full, 0) &&
+                wait_all(&qdo_full[0], 0);
       if (ok) {
         tc_fence_after();
         issue_s(0);
-        mma_commit(s_ready);
+        mma_commit_e(s_ready);
         issue_dp(0);
-        mma_commit(dp_ready);
+        mma_commit_e(dp_ready);
       }
       for (int i = 0; i < nq && ok; ++i) {
         const int s = i % NQS, s1 = (i + 1) % NQS;
@@ -386,39 +390,39 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
         const uint32_t acc0 = i > 0 ? 1u : 0u;
         const bool next = i + 1 < nq;
         // dV += P^T dO, then the next block's S^T
-        if (!mbar_wait_bounded(p_ready, i & 1, abort_flag, a.spin_limit)) { ok = false; break; }
+        if (!wait_all(p_ready, i & 1)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kBlk / 16; ++kk)
-          mma_ts(tmem + C::kDV, tmem + C::kST + packed_col(kk), o_mn0 + so + kk * attn::kKRowStep, id_nd, kk > 0 ? 1u : acc0);
+          mma_ts_e(tmem + C::kDV, tmem + C::kST + packed_col(kk), o_mn0 + so + kk * attn::kKRowStep, id_nd, kk > 0 ? 1u : acc0);
         if (next) {
-          if (!mbar_wait_bounded(&qdo_full[s1], ((i + 1) / NQS) & 1, abort_flag, a.spin_limit)) { ok = false; break; }
+          if (!wait_all(&qdo_full[s1], ((i + 1) / NQS) & 1)) { ok = false; break; }
           tc_fence_after();
           issue_s(s1);
-          mma_commit(s_ready);
+          mma_commit_e(s_ready);
         }
         // dK += dS^T Q, dQ = dS K (dQ's TMEM columns drained), then the next block's dP^T
-        if (!mbar_wait_bounded(ds_ready, i & 1, abort_flag, a.spin_limit)) { ok = false; break; }
+        if (!wait_all(ds_ready, i & 1)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kBlk / 16; ++kk)
-          mma_ts(tmem + C::kDK, tmem + C::kDPT + packed_col(kk), q_mn0 + so + kk * attn::kKRowStep, id_nd, kk > 0 ? 1u : acc0);
-        mma_commit(&qdo_empty[s]);   // Q and dO of this block are no longer read (dQ uses dS and K)
-        if (i > 0 && !mbar_wait_bounded(dq_free, (i - 1) & 1, abort_flag, a.spin_limit)) { ok = false; break; }
+          mma_ts_e(tmem + C::kDK, tmem + C::kDPT + packed_col(kk), q_mn0 + so + kk * attn::kKRowStep, id_nd, kk > 0 ? 1u : acc0);
+        mma_commit_e(&qdo_empty[s]);   // Q and dO of this block are no longer read (dQ uses dS and K)
+        if (i > 0 && !wait_all(dq_free, (i - 1) & 1)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kBlk / 16; ++kk)
-          mma_ss(tmem + C::kDQ, ds_d + kk * kDsRows, k_mn + kk * attn::kKRowStep, id_dq, kk > 0 ? 1u : 0u);
-        mma_commit(dq_ready);
+          mma_ss_e(tmem + C::kDQ, ds_d + kk * kDsRows, k_mn + kk * attn::kKRowStep, id_dq, kk > 0 ? 1u : 0u);
+        mma_commit_e(dq_ready);
         if (next) {
           issue_dp(s1);
-          mma_commit(dp_ready);
+          mma_commit_e(dp_ready);
         }
       }
-      if (ok) mma_commit(kdv_done);
+      if (ok) mma_commit_e(kdv_done);
       else watchdog_fire(kWdBwdMma);
       // Drain: every MMA issued above has completed before TMEM is released.
-      mma_commit(drain);
+      mma_commit_e(drain);
       for (uint32_t it = 0; it < a.spin_limit && !mbar_try_wait(drain, 0); ++it) {
       }
     }
