@@ -97,6 +97,7 @@ struct BwdArgs {
   const float* delta;
   float* dq_acc;          // [B*S, H*D] fp32 (the main kernel adds into it through its tensor map)
   float* dbias_part;      // [B*H, n_kb, n_qb, kWarpsPerTile, kBins]
+  float* dpd_rows;        // [H, 2 n_blk - 1, 256]: per tile-diagonal sums (dBias reduction stage 1)
   void* dqkv;
   int64_t dqkv_stride;
   int B, S, H, D, n_blk;
@@ -669,37 +670,43 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
   if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
 }
 
-// delta[b*H + h, s] = sum_d dO * O32; zero the dQ accumulator.  One thread per (token, head).
+// delta[b*H + h, s] = sum_d dO * O32; zero the dQ accumulator.  A CTA takes 32 consecutive
+// (token, head) pairs, i.e. 32 * D contiguous elements of dO / O32 / dQ, one 8-element chunk per
+// thread (fully coalesced 16- and 32-byte accesses); each pair's D/8 chunk products are then summed
+// in chunk order from shared memory.
 template <bool F16>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(32 * 16)
 relpos_bwd_prep_kernel(const void* __restrict__ dout, const float* __restrict__ out32, float* __restrict__ delta,
-                       float* __restrict__ dq_acc, int B, int S, int H, int D) {
+                       float* __restrict__ dq_acc, int64_t pairs, int S, int H, int cph) {
   using T = typename std::conditional<F16, __half, __nv_bfloat16>::type;
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // token * H + head
-  if (idx >= (int64_t)B * S * H) return;
-  const int64_t tok = idx / H;
-  const int hh = (int)(idx % H);
-  const size_t off = (size_t)tok * H * D + (size_t)hh * D;
-  const T* g = reinterpret_cast<const T*>(dout) + off;
-  const float* o = out32 + off;
-  float* z = dq_acc + off;
+  __shared__ float part[32 * 16];
+  const int64_t p0 = (int64_t)blockIdx.x * 32;
+  const int64_t c = p0 * cph + threadIdx.x;   // this thread's 8-element chunk
   float acc = 0.f;
-  for (int d = 0; d < D; d += 8) {
-    const uint4 gv = *reinterpret_cast<const uint4*>(g + d);
-    const float4 o0 = *reinterpret_cast<const float4*>(o + d);
-    const float4 o1 = *reinterpret_cast<const float4*>(o + d + 4);
+  if (c < pairs * cph) {
+    const uint4 gv = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(dout) + 8 * c);
+    const float4 o0 = *reinterpret_cast<const float4*>(out32 + 8 * c);
+    const float4 o1 = *reinterpret_cast<const float4*>(out32 + 8 * c + 4);
     const T* gt = reinterpret_cast<const T*>(&gv);
     float gf[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) gf[k] = F16 ? __half2float(*reinterpret_cast<const __half*>(&gt[k]))
                                             : __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(&gt[k]));
-    acc += gf[0] * o0.x + gf[1] * o0.y + gf[2] * o0.z + gf[3] * o0.w;
+    acc = gf[0] * o0.x + gf[1] * o0.y + gf[2] * o0.z + gf[3] * o0.w;
     acc += gf[4] * o1.x + gf[5] * o1.y + gf[6] * o1.z + gf[7] * o1.w;
-    *reinterpret_cast<float4*>(z + d) = make_float4(0.f, 0.f, 0.f, 0.f);
-    *reinterpret_cast<float4*>(z + d + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+    *reinterpret_cast<float4*>(dq_acc + 8 * c) = make_float4(0.f, 0.f, 0.f, 0.f);
+    *reinterpret_cast<float4*>(dq_acc + 8 * c + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  const int b = (int)(tok / S), s = (int)(tok % S);
-  delta[((size_t)b * H + hh) * S + s] = acc;
+  part[threadIdx.x] = acc;
+  __syncthreads();
+  const int64_t pr = p0 + threadIdx.x;
+  if (threadIdx.x < 32 && pr < pairs) {
+    float s = 0.f;
+    for (int k = 0; k < cph; ++k) s += part[threadIdx.x * cph + k];
+    const int64_t tok = pr / H;
+    const int hh = (int)(pr % H);
+    delta[((tok / S) * H + hh) * S + tok % S] = s;
+  }
 }
 
 // dqkv[:, q section] = dQ accumulator * scale, rounded to the input dtype.
@@ -724,39 +731,56 @@ relpos_bwd_dq_kernel(const float* __restrict__ dq_acc, void* __restrict__ dqkv, 
   *reinterpret_cast<uint4*>(reinterpret_cast<T*>(dqkv) + row * dqkv_stride + c) = pk;
 }
 
-// dpd[h, t] = sum over b, over the tiles (kb, qb) whose diagonal range covers g = t - (S-1) =
-// key - query, and over the eight (query half, key quarter) warps of each tile, of the bin holding
-// g.  A tile at offset d = kb - qb holds tile diagonal e = g - 128 d; warp (half, quarter) holds it
-// in bin 32 quarter - 64 half + 31 - e.  Fixed order: deterministic.
+// dBias reduction, stage 1: one CTA per (tile diagonal d = kb - qb, head h).  Thread (w, j) sums
+// bin j of warp w over the batch and the tiles on diagonal d (each tile's 8 x 96 bins are one
+// contiguous 3 KB row, so the CTA's loads are coalesced); then, per tile diagonal e = key - query in
+// [-127, 127], the bins holding e (warp (half, quarter) keeps e in bin 32 quarter - 64 half + 31 - e)
+// are added in warp order.  rows[h, d + nb - 1, e + 127].  Fixed order: deterministic.
+constexpr int kDiagThreads = kWarpsPerTile * kBins;   // 768
+__global__ void __launch_bounds__(kDiagThreads)
+relpos_bwd_dpd_diag_kernel(const float* __restrict__ part, float* __restrict__ rows, int B, int H, int nb) {
+  __shared__ float acc[kDiagThreads];
+  const int d = (int)blockIdx.x - (nb - 1), h = blockIdx.y;
+  const int kb_lo = d > 0 ? d : 0, kb_hi = d > 0 ? nb : nb + d;   // qb = kb - d in [0, nb)
+  float s = 0.f;
+  for (int bb = 0; bb < B; ++bb) {
+    const float* pb = part + (size_t)(bb * H + h) * nb * nb * kDiagThreads;
+    for (int kb = kb_lo; kb < kb_hi; ++kb) s += __ldg(pb + ((size_t)kb * nb + (kb - d)) * kDiagThreads + threadIdx.x);
+  }
+  acc[threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.x < 2 * kBlk - 1) {
+    const int e = (int)threadIdx.x - (kBlk - 1);
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarpsPerTile; ++w) {
+      const int j = 32 * (w % 4) - 64 * (w / 4) + 31 - e;
+      if (j >= 0 && j < kBins) v += acc[w * kBins + j];
+    }
+    rows[((size_t)h * (2 * nb - 1) + blockIdx.x) * 256 + threadIdx.x] = v;
+  }
+}
+
+// dBias reduction, stage 2: dpd[h, t] for g = t - (S - 1) = key - query: the two tile diagonals
+// whose range covers g (d_hi = ceil-ish (g - 127) / 128 and d_hi - 1), added in that order.
 __global__ void __launch_bounds__(256)
-relpos_bwd_dpd_kernel(const float* __restrict__ part, float* __restrict__ dpd, int B, int S, int H, int nb) {
+relpos_bwd_dpd_kernel(const float* __restrict__ rows, float* __restrict__ dpd, int S, int H, int nb) {
   const int h = blockIdx.y;
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= 2 * S - 1) return;
   const int g = t - (S - 1);
   const int d_hi = (g + 127) >= 0 ? (g + 127) / 128 : -((-(g + 127) + 127) / 128);
   float acc = 0.f;
-  for (int bb = 0; bb < B; ++bb) {
-    const float* pb = part + (size_t)(bb * H + h) * nb * nb * kWarpsPerTile * kBins;
-    for (int d = d_hi; d >= d_hi - 1; --d) {
-      const int e = g - 128 * d;
-      if (e < -(kBlk - 1) || e > kBlk - 1) continue;
-      const int kb_lo = d > 0 ? d : 0, kb_hi = d > 0 ? nb : nb + d;   // qb = kb - d in [0, nb)
-      for (int kbi = kb_lo; kbi < kb_hi; ++kbi) {
-        const float* tile = pb + ((size_t)kbi * nb + (kbi - d)) * kWarpsPerTile * kBins;
-#pragma unroll
-        for (int w = 0; w < kWarpsPerTile; ++w) {
-          const int j = 32 * (w % 4) - 64 * (w / 4) + 31 - e;
-          if (j >= 0 && j < kBins) acc += tile[w * kBins + j];
-        }
-      }
-    }
+  for (int d = d_hi; d >= d_hi - 1; --d) {
+    const int e = g - 128 * d;
+    if (e < -(kBlk - 1) || e > kBlk - 1 || d <= -nb || d >= nb) continue;
+    acc += rows[((size_t)h * (2 * nb - 1) + (d + nb - 1)) * 256 + (e + kBlk - 1)];
   }
   dpd[(size_t)h * (2 * S - 1) + t] = acc;
 }
 
 struct WsLayout {
-  size_t delta, dq, part, total;
+  size_t delta, dq, part, rows, total;
 };
 
 inline WsLayout ws_layout(int64_t B, int64_t S, int64_t H, int64_t D) {
@@ -766,7 +790,8 @@ inline WsLayout ws_layout(int64_t B, int64_t S, int64_t H, int64_t D) {
   w.delta = 0;
   w.dq = up((size_t)B * H * S * 4);
   w.part = w.dq + up((size_t)B * S * H * D * 4);
-  w.total = w.part + up((size_t)B * H * nb * nb * kWarpsPerTile * kBins * 4);
+  w.rows = w.part + up((size_t)B * H * nb * nb * kWarpsPerTile * kBins * 4);
+  w.total = w.rows + up((size_t)H * (2 * nb - 1) * 256 * 4);
   return w;
 }
 
@@ -775,8 +800,8 @@ int launch_bwd(const CUtensorMap& qm, const CUtensorMap& om, const CUtensorMap& 
                const float* out32, float* dpd, cudaStream_t stream) {
   using C = BwdCfg<DP>;
   const int64_t tokens_heads = (int64_t)a.B * a.S * a.H;
-  relpos_bwd_prep_kernel<F16><<<(unsigned)((tokens_heads + 255) / 256), 256, 0, stream>>>(
-      dout, out32, const_cast<float*>(a.delta), a.dq_acc, a.B, a.S, a.H, a.D);
+  relpos_bwd_prep_kernel<F16><<<(unsigned)((tokens_heads + 31) / 32), 32 * (a.D / 8), 0, stream>>>(
+      dout, out32, const_cast<float*>(a.delta), a.dq_acc, tokens_heads, a.S, a.H, a.D / 8);
   KRSI_LAUNCH_CHECK();
   const size_t res_smem = C::kSmem + (size_t)rows_bytes(a.S);
   const bool res = res_smem <= 232448;   // 227 KB per CTA on sm_100
@@ -792,8 +817,10 @@ int launch_bwd(const CUtensorMap& qm, const CUtensorMap& om, const CUtensorMap& 
   relpos_bwd_dq_kernel<F16><<<(unsigned)((items + 255) / 256), 256, 0, stream>>>(a.dq_acc, a.dqkv, a.dqkv_stride,
                                                                                   rows, a.H * a.D, a.scale);
   KRSI_LAUNCH_CHECK();
-  relpos_bwd_dpd_kernel<<<dim3((2 * a.S - 1 + 255) / 256, a.H), 256, 0, stream>>>(a.dbias_part, dpd, a.B, a.S, a.H,
-                                                                                   a.n_blk);
+  relpos_bwd_dpd_diag_kernel<<<dim3(2 * a.n_blk - 1, a.H), kDiagThreads, 0, stream>>>(a.dbias_part, a.dpd_rows, a.B,
+                                                                                      a.H, a.n_blk);
+  KRSI_LAUNCH_CHECK();
+  relpos_bwd_dpd_kernel<<<dim3((2 * a.S - 1 + 255) / 256, a.H), 256, 0, stream>>>(a.dpd_rows, dpd, a.S, a.H, a.n_blk);
   KRSI_LAUNCH_CHECK();
   return KRSI_OK;
 }
@@ -854,6 +881,7 @@ extern "C" int krsi_relpos_attn_bwd(const void* dout, const void* qkv, int64_t q
             reinterpret_cast<float*>(w + ws.delta),
             reinterpret_cast<float*>(w + ws.dq),
             reinterpret_cast<float*>(w + ws.part),
+            reinterpret_cast<float*>(w + ws.rows),
             dqkv,
             dqkv_row_stride,
             (int)B,
