@@ -80,9 +80,15 @@ struct FwdArgs {
 // Resident bias row: pd[h, :] * log2(e) with kRowPad zeros before it and 128 after, so every
 // index a CTA forms (key - query + S - 1 for keys and queries up to 127 past S) stays inside.
 // Two copies, the second shifted by one element, so that every thread reads its 128 bias values
-// as 8-byte aligned pairs (copy 0 when its start index is even, copy 1 when odd).
+// as 8-byte aligned pairs (copy 0 when its start index is even, copy 1 when odd).  Lane l of a warp
+// starts at B0 - l with B0 of the parity of S - 1; in a half-warp the copy-0 lanes then read 16
+// consecutive floats and the copy-1 lanes 16 more, shifted by the copy distance - 16 (S even) or
+// - 18 (S odd).  Spacing the copies 16 or 18 (mod 32) floats apart puts the two halves on disjoint
+// banks: one wavefront per half-warp.
 constexpr int kRowPad = 256;
-__host__ __device__ constexpr int64_t row_floats(int64_t S) { return (2 * S - 1 + kRowPad + 128 + 1) / 2 * 2; }
+__host__ __device__ constexpr int64_t row_floats(int64_t S) {
+  return (2 * S - 1 + kRowPad + 128 + 31 - ((S & 1) ? 18 : 16)) / 32 * 32 + ((S & 1) ? 18 : 16);
+}
 __host__ __device__ constexpr int64_t row_bytes(int64_t S) { return 2 * row_floats(S) * 4; }
 
 
