@@ -108,8 +108,20 @@ rms_fwd_kernel(const typename Elem<XT>::T* __restrict__ x, const typename Elem<W
   }
 }
 
+// Warp-per-row plans with up to 40 elements per thread keep their running dw sums in shared memory
+// (lane-interleaved float4s: conflict-free) instead of registers, which fits two 256-thread blocks
+// per SM: twice the rows in flight for a latency-bound backward.  The sums are the same fmaf chain
+// in the same row order, so dw is bitwise unchanged.
+template <int TPR, int VEC, int NCH>
+constexpr bool kBwdSmemAcc = TPR == 32 && NCH * VEC <= 40 && VEC % 4 == 0;
+template <int TPR, int VEC, int NCH>
+constexpr int kBwdMinBlocks = kBwdSmemAcc<TPR, VEC, NCH> ? 2 : 1;
+// index of (chunk c, element e) of lane t in a warp's interleaved accumulator
+template <int VEC>
+__device__ __forceinline__ int acc_idx(int c, int e, int t) { return ((c * (VEC / 4) + e / 4) * 32 + t) * 4 + e % 4; }
+
 template <int XT, int WT, int TPR, int VEC, int NCH>
-__global__ void __launch_bounds__(RowCfg<TPR>::kThreads)
+__global__ void __launch_bounds__(RowCfg<TPR>::kThreads, kBwdMinBlocks<TPR, VEC, NCH>)
 rms_bwd_kernel(const typename Elem<XT>::T* __restrict__ g, const typename Elem<XT>::T* __restrict__ x,
                const typename Elem<WT>::T* __restrict__ w, const float* __restrict__ rstd,
                typename Elem<XT>::T* __restrict__ dx, float* __restrict__ dw_part, int64_t rows, int n) {
@@ -121,11 +133,19 @@ rms_bwd_kernel(const typename Elem<XT>::T* __restrict__ g, const typename Elem<X
   const int t = threadIdx.x % TPR;
   const int sub = threadIdx.x / TPR;
 
+  constexpr bool SACC = kBwdSmemAcc<TPR, VEC, NCH>;
   float dwv[NCH][VEC];
 #pragma unroll
   for (int c = 0; c < NCH; ++c)
 #pragma unroll
     for (int e = 0; e < VEC; ++e) dwv[c][e] = 0.f;
+  float4* acc4 = reinterpret_cast<float4*>(smem_dw + sub * (NCH * VEC * 32));   // SACC: this warp's sums
+  if constexpr (SACC) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c)
+#pragma unroll
+      for (int e = 0; e < VEC; e += 4) acc4[acc_idx<VEC>(c, e, t) / 4] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
 
   for (int64_t row0 = (int64_t)blockIdx.x * RPB; row0 < rows; row0 += (int64_t)gridDim.x * RPB) {
     const int64_t row = row0 + sub;
@@ -155,10 +175,23 @@ rms_bwd_kernel(const typename Elem<XT>::T* __restrict__ g, const typename Elem<X
 #pragma unroll
         for (int e = 0; e < VEC; ++e) wv[e] = 0.f;
       }
+      if constexpr (SACC) {
+        if (live && col < n) {
+#pragma unroll
+          for (int e = 0; e < VEC; e += 4) {
+            float4 s = acc4[acc_idx<VEC>(c, e, t) / 4];
+            s.x = fmaf(dn[c][e], WE::round(xv[c][e] * r), s.x);
+            s.y = fmaf(dn[c][e + 1], WE::round(xv[c][e + 1] * r), s.y);
+            s.z = fmaf(dn[c][e + 2], WE::round(xv[c][e + 2] * r), s.z);
+            s.w = fmaf(dn[c][e + 3], WE::round(xv[c][e + 3] * r), s.w);
+            acc4[acc_idx<VEC>(c, e, t) / 4] = s;
+          }
+        }
+      }
 #pragma unroll
       for (int e = 0; e < VEC; ++e) {
         const float gg = dn[c][e];
-        dwv[c][e] = fmaf(gg, WE::round(xv[c][e] * r), dwv[c][e]);
+        if constexpr (!SACC) dwv[c][e] = fmaf(gg, WE::round(xv[c][e] * r), dwv[c][e]);
         dn[c][e] = DE::round(gg * wv[e]);
         dot = fmaf(dn[c][e], xv[c][e], dot);
       }
@@ -182,20 +215,29 @@ rms_bwd_kernel(const typename Elem<XT>::T* __restrict__ g, const typename Elem<X
 
   // Per-block dw partial; the RPB row groups of a block are combined in a fixed order.
   float* out = dw_part + (int64_t)blockIdx.x * n;
-  float* dst = RPB == 1 ? out : smem_dw + sub * n;
+  if constexpr (!SACC) {
+    float* dst = RPB == 1 ? out : smem_dw + sub * n;
 #pragma unroll
-  for (int c = 0; c < NCH; ++c)
+    for (int c = 0; c < NCH; ++c)
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) {
-      const int col = (c * TPR + t) * VEC + e;
-      if (col < n) dst[col] = dwv[c][e];
-    }
+      for (int e = 0; e < VEC; ++e) {
+        const int col = (c * TPR + t) * VEC + e;
+        if (col < n) dst[col] = dwv[c][e];
+      }
+  }
   if constexpr (RPB > 1) {
     __syncthreads();
     for (int col = threadIdx.x; col < n; col += blockDim.x) {
       float s = 0.f;
+      if constexpr (SACC) {
+        const int c = col / (TPR * VEC), rem = col % (TPR * VEC);
+        const int idx = acc_idx<VEC>(c, rem % VEC, rem / VEC);
 #pragma unroll
-      for (int i = 0; i < RPB; ++i) s += smem_dw[i * n + col];
+        for (int i = 0; i < RPB; ++i) s += smem_dw[i * (NCH * VEC * 32) + idx];
+      } else {
+#pragma unroll
+        for (int i = 0; i < RPB; ++i) s += smem_dw[i * n + col];
+      }
       out[col] = s;
     }
   }
@@ -261,7 +303,7 @@ struct Plan {
 inline int elem_size(int dt) { return dt == KRSI_F32 ? 4 : 2; }
 
 // Warp-per-row chunk counts that are compiled; a needed count is rounded up to the next.
-constexpr int kWarpNch[] = {1, 2, 3, 4, 6, 8, 9, 12, 16};
+constexpr int kWarpNch[] = {1, 2, 3, 4, 5, 6, 8, 9, 12, 16};
 constexpr int kBlockNch[] = {1, 2, 4, 8, 16};
 
 inline bool plan_rows(int64_t n, int x_dtype, bool vec_ok, Plan* p) {
@@ -306,7 +348,8 @@ int run_fwd(const FwdArgs& a) {
 template <int XT, int WT, int TPR, int VEC, int NCH>
 int run_bwd(const BwdArgs& a) {
   using Cfg = RowCfg<TPR>;
-  const size_t smem = Cfg::kRowsPerBlock > 1 ? (size_t)Cfg::kRowsPerBlock * a.n * sizeof(float) : 0;
+  const size_t per_warp = kBwdSmemAcc<TPR, VEC, NCH> ? (size_t)NCH * VEC * 32 : (size_t)a.n;
+  const size_t smem = Cfg::kRowsPerBlock > 1 ? (size_t)Cfg::kRowsPerBlock * per_warp * sizeof(float) : 0;
   auto kern = rms_bwd_kernel<XT, WT, TPR, VEC, NCH>;
   if (smem > 48 * 1024)
     KRSI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -328,7 +371,7 @@ int dispatch_shape(const Plan& p, const Args& a) {
   if (p.tpr == 32) {
     switch (p.nch) {
       case 1: KRSI_RUN(32, 1); case 2: KRSI_RUN(32, 2); case 3: KRSI_RUN(32, 3);
-      case 4: KRSI_RUN(32, 4); case 6: KRSI_RUN(32, 6); case 8: KRSI_RUN(32, 8);
+      case 4: KRSI_RUN(32, 4); case 5: KRSI_RUN(32, 5); case 6: KRSI_RUN(32, 6); case 8: KRSI_RUN(32, 8);
       case 9: KRSI_RUN(32, 9); case 12: KRSI_RUN(32, 12); case 16: KRSI_RUN(32, 16);
     }
   } else if (p.tpr == 256) {
