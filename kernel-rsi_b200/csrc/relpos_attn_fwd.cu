@@ -47,6 +47,7 @@ constexpr uint32_t kRegsSm = 200;   // softmax warpgroups (launch 168 x 384 >= 1
 constexpr int kSlab = 384;          // floats per bias slab (2*128 + 128 - 1 = 383 used)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;   // log2 units: P <= 2^8 between rescales
+constexpr int kRowFillers = 320;           // warps 2-11 fill the resident bias window
 
 template <int DP>
 struct FwdCfg {
@@ -93,6 +94,14 @@ __host__ __device__ constexpr int64_t row_bytes(int64_t S) { return 2 * row_floa
 
 
 
+// dst[i] = src[i - pad] * log2(e) for i in [w0, w1), zero where i - pad is outside [0, len), by
+// kRowFillers cooperating threads.
+__device__ __forceinline__ void fill_row_window(float* dst, int w0, int w1, int pad, const float* __restrict__ src,
+                                                int len, int tid) {
+  const int s0 = max(w0 - pad, 0), s1 = min(w1 - pad, len);
+  attn::fill_row(dst + w0, w1 - w0, s0 + pad - w0, src + s0, max(s1 - s0, 0), kLog2e, tid, kRowFillers);
+}
+
 template <int DP, bool F16, bool RES>
 __global__ void __launch_bounds__(kThreads, 1)
 relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
@@ -132,7 +141,7 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
       mbar_init(&o_final[t], 1);
     }
     mbar_init(drain, 1);
-    mbar_init(row_full, 64);
+    mbar_init(row_full, kRowFillers);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -145,6 +154,20 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Resident bias window (RES), filled by warps 2-11 (the softmax warps are idle until their first
+  // S tile): only the indices this CTA forms, kRowPad + key - query + S - 1 for its 256 queries and
+  // all keys, plus one on each side for the shifted copy.
+  auto fill_window = [&]() {
+    const int two_s = 2 * a.S - 1;
+    const float* pdh = a.pd + (size_t)h * two_s;
+    const int n = (int)row_floats(a.S);
+    const int tid = threadIdx.x - 64;
+    const int w0 = max(kRowPad + a.S - 1 - (q0 + kQTiles * kTileRows - 1) - 1, 0);
+    const int w1 = min(kRowPad + a.S - 1 - q0 + n_kb * kBN + 1, n);
+    fill_row_window(row0, w0, w1, kRowPad, pdh, two_s, tid);
+    fill_row_window(row1, w0, w1, kRowPad - 1, pdh, two_s, tid);   // row1[i] = row0[i + 1]
+    mbar_arrive(row_full);
+  };
   // Each role runs entirely inside the branch that sets its register budget, so ptxas compiles
   // it against that budget.
   if (warp < 4) {
@@ -183,16 +206,8 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
       if (lane == 0) mbar_arrive(&kv_full[s]);
     }
   } else if (warp == 2 || warp == 3) {
-    // ------------------------------------------------------------ resident bias rows (RES)
-    if constexpr (RES) {
-      const int two_s = 2 * a.S - 1;
-      const float* pdh = a.pd + (size_t)h * two_s;
-      const int n = (int)row_floats(a.S);
-      const int tid = threadIdx.x - 64;
-      attn::fill_row(row0, n, kRowPad, pdh, two_s, kLog2e, tid, 64);
-      attn::fill_row(row1, n, kRowPad - 1, pdh, two_s, kLog2e, tid, 64);   // row1[i] = row0[i + 1]
-      mbar_arrive(row_full);
-    }
+    // ------------------------------------------------------------ resident bias window (RES)
+    if constexpr (RES) fill_window();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -264,6 +279,7 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
   }
   } else {
     regs_inc<kRegsSm>();
+    if constexpr (RES) fill_window();
     // ------------------------------------------------------------ softmax (warps 4..11)
     const int t = (warp - 4) / 4;                       // query tile
     const int quarter = warp % 4;                       // TMEM lane quarter of this warp
