@@ -21,17 +21,18 @@
 //                              S^T = K Q^T, dP^T = V dO^T              (SS, K = DP)
 //                              dV += P^T dO, dK += dS^T Q               (TS: P^T/dS^T in TMEM)
 //                              dQ  = dS K                              (SS: dS staged in smem)
-//                warps 2-3   (with warps 12-15) the resident bias rows: a reversed window of the
-//                            bias row, in two copies (the second shifted by one, for aligned pairs)
+//                warps 2-15  first fill the resident bias rows: a reversed window of the bias
+//                            row, in two copies (the second shifted by one, for aligned pairs)
 //                warps 4-11  two compute warpgroups, one key row per thread and 64 queries per
 //                            warpgroup: P^T, dS^T in paired fp32 -> 16-bit into TMEM and smem;
 //                            dBias diagonal sums of the fp32 dS by a warp-shuffle transpose into
-//                            per-lane register bins (no S x S buffer, no atomics)
+//                            per-lane register bins (no S x S buffer, no atomics); at the end dK
+//                            (warpgroup 0) and dV (warpgroup 1) -> dqkv
 //                warps 12-15 one query row per thread: dQ tile from TMEM -> a shared-memory tile
-//                            that one TMA reduce-add sums into the fp32 accumulator; at the end
-//                            dK, dV -> dqkv
+//                            that one TMA reduce-add sums into the fp32 accumulator
 //   bwd_dq     dQ accumulator * scale -> dqkv (input dtype)
-//   bwd_dpd    dpd[h, t] = fixed-order sum of the per-tile diagonal partials (deterministic)
+//   bwd_dpd    dpd[h, t] = fixed-order sums of the per-tile diagonal partials, per tile diagonal
+//              then per output (deterministic)
 // dK, dV and dpd are bitwise reproducible; dQ sums per-key-block fp32 partials in arrival
 // order (like FlashAttention's dQ accumulation), so its last bits can vary run to run.
 #include <string.h>
@@ -62,7 +63,7 @@ constexpr uint32_t kRegsCompute = 160;
 constexpr uint32_t kRegsDq = 88;
 constexpr int kWarpsPerTile = 8;    // dBias partial rows per tile: (query half, key quarter)
 constexpr int kBins = 96;           // per-warp bins: 32 keys x 64 queries -> 95 diagonals (+1 zero)
-constexpr int kRowFillers = 192;    // warps 2-3 and 12-15 fill the resident rows
+constexpr int kRowFillers = 448;    // warps 2-15 fill the resident rows (compute warps: before their first P)
 constexpr int kCopyBank = 16;       // distance (mod 32 floats) between the two bias copies
 
 constexpr float kLog2e = 1.4426950408889634f;
@@ -221,6 +222,37 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
     attn::fill_row_rev(rev0, n, top, pdh, lo, hi, kLog2e, tid, kRowFillers);
     attn::fill_row_rev(rev1, n, top - 1, pdh, lo, hi, kLog2e, tid, kRowFillers);
     mbar_arrive(row_full);
+  };
+
+  // dK (scaled) or dV of key row kr, TMEM -> dqkv; run by one compute warpgroup each at the end.
+  auto store_dkdv = [&](const int which, const int kr, const uint32_t lane_addr) {
+    using T = typename std::conditional<F16, __half, __nv_bfloat16>::type;
+    const int key = k0 + kr;
+    const bool row_ok = key < a.S;
+    T* dst = reinterpret_cast<T*>(a.dqkv) + ((size_t)b * a.S + (row_ok ? key : 0)) * a.dqkv_stride +
+             (size_t)(1 + which) * a.H * a.D + (size_t)h * a.D;
+    const uint32_t src = tmem + lane_addr + (which == 0 ? C::kDK : C::kDV);
+    const float mul = which == 0 ? a.scale : 1.f;
+#pragma unroll
+    for (int c = 0; c < DP; c += 16) {
+      uint32_t u[16];
+      tmem_ld16(src + c, u);
+      tmem_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 16; e += 8) {
+        if (row_ok && c + e < a.D) {
+          float f[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) f[k] = __uint_as_float(u[e + k]) * mul;
+          const uint4 pk =
+              F16 ? make_uint4(pack_f16x2(f[0], f[1]), pack_f16x2(f[2], f[3]), pack_f16x2(f[4], f[5]),
+                               pack_f16x2(f[6], f[7]))
+                  : make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                               pack_bf16x2(f[6], f[7]));
+          *reinterpret_cast<uint4*>(dst + c + e) = pk;
+        }
+      }
+    }
   };
 
   // Each role runs entirely inside the branch that sets its register budget.
@@ -430,6 +462,7 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
   }
   } else if (warp < 12) {
     regs_inc<kRegsCompute>();
+    if constexpr (RES) fill_rows(threadIdx.x - 64);
     // ------------------------------------------------------------ compute: one key x 64 queries per thread
     const int quarter = warp % 4, half = (warp - 4) / 4;
     const int kr = quarter * 32 + lane;        // key row within the block (TMEM lane)
@@ -567,10 +600,18 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
 #pragma unroll
       for (int k = 0; k < 3; ++k) out[31 - lane + 32 * k] = dbin[k];
     }
-    if (!ok) watchdog_fire(kWdBwdCompute);
+    // dK (warpgroup 0) or dV (warpgroup 1) of this key row -> dqkv, while warps 12-15 drain the
+    // last dQ tile
+    if (ok && !__all_sync(0xffffffffu, mbar_wait_bounded(kdv_done, 0, abort_flag, a.spin_limit))) ok = false;
+    if (!ok) {
+      watchdog_fire(kWdBwdCompute);
+    } else {
+      tc_fence_after();
+      store_dkdv(half, kr, lane_addr);
+    }
   } else {
     regs_dec<kRegsDq>();
-    if constexpr (RES) fill_rows(threadIdx.x - 384 + 64);
+    if constexpr (RES) fill_rows(threadIdx.x - 64);
     // ------------------------------------------------------------ dQ WG: one query row per thread
     const int quarter = warp % 4;
     const int r = quarter * 32 + lane;
@@ -623,45 +664,7 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
       }
     }
     if (leader) bulk_wait_all();
-    // dK, dV (rows = keys) -> dqkv
-    if (ok && !__all_sync(0xffffffffu, mbar_wait_bounded(kdv_done, 0, abort_flag, a.spin_limit))) ok = false;
-    if (!ok) {
-      watchdog_fire(kWdBwdDq);
-    } else {
-      tc_fence_after();
-      using T = typename std::conditional<F16, __half, __nv_bfloat16>::type;
-      const int key = k0 + r;
-      const bool row_ok = key < a.S;
-      T* base = reinterpret_cast<T*>(a.dqkv) + ((size_t)b * a.S + (row_ok ? key : 0)) * a.dqkv_stride;
-#pragma unroll
-      for (int which = 0; which < 2; ++which) {   // 0: dK (scaled), 1: dV
-        const uint32_t src = tmem + lane_addr + (which == 0 ? C::kDK : C::kDV);
-        T* dst = base + (size_t)(1 + which) * a.H * a.D + (size_t)h * a.D;
-        const float mul = which == 0 ? a.scale : 1.f;
-#pragma unroll
-        for (int c = 0; c < DP; c += 16) {
-          uint32_t u[16];
-          tmem_ld16(src + c, u);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 16; e += 8) {
-            if (row_ok && c + e < a.D) {
-              uint4 pk;
-              float f[8];
-#pragma unroll
-              for (int k = 0; k < 8; ++k) f[k] = __uint_as_float(u[e + k]) * mul;
-              if (F16)
-                pk = make_uint4(pack_f16x2(f[0], f[1]), pack_f16x2(f[2], f[3]), pack_f16x2(f[4], f[5]),
-                                pack_f16x2(f[6], f[7]));
-              else
-                pk = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
-                                pack_bf16x2(f[6], f[7]));
-              *reinterpret_cast<uint4*>(dst + c + e) = pk;
-            }
-          }
-        }
-      }
-    }
+    if (!ok) watchdog_fire(kWdBwdDq);
   }
 
   tc_fence_before();
