@@ -59,9 +59,11 @@ __device__ __forceinline__ void load_tile(uint8_t* smem_tile, const CUtensorMap*
 // Fills dst[i] = src[i - pad] * mul for i in [0, n), zero where i - pad is outside [0, len).  Run by
 // `nthr` cooperating threads (tid in [0, nthr)); the 16-byte-aligned interior of src is read with
 // 128-bit loads, four in flight per thread, so a row of a few thousand floats takes one or two
-// memory round trips.  dst may have any 4-byte alignment.
+// memory round trips.  dst may have any 4-byte alignment.  Source elements that would land at or
+// past dst[n] are not read (len is clipped to n - pad).
 __device__ __forceinline__ void fill_row(float* dst, int n, int pad, const float* __restrict__ src, int len, float mul,
                                          int tid, int nthr) {
+  len = min(len, max(n - pad, 0));
   const int mis = (int)((reinterpret_cast<uintptr_t>(src) >> 2) & 3);
   const int a0 = mis ? min(4 - mis, len) : 0;         // first 16-byte aligned source index
   const int nvec = len > a0 ? (len - a0) / 4 : 0;

@@ -5,22 +5,26 @@
 //   m_i = max_j s2, l_i = sum_j exp2(s2 - m_i), out_i = sum_j exp2(s2 - m_i) v_j / l_i,
 //   lse_i = m_i + log2(l_i); out in the input dtype, out32 in fp32.
 //
-// Structure (one CTA = two 128-query tiles of one (b, h), 12 warps = 3 warpgroups; setmaxnreg
-// moves registers from warpgroup 0 to the softmax warpgroups):
-//   warp 0      TMA producer (tile layout: attn_common.cuh): Q once, then per 128-key block a K
-//               tile and a V tile (3-stage ring);
-//   warps 2-3   the bias row pd[h, :] * log2(e), resident in shared memory for the CTA's life
-//               (two copies, one shifted by an element, for aligned pair reads), fetched with
-//               128-bit loads; sequences too long for it fall back to a per-block slab the
-//               producer writes;
+// Structure: a persistent grid (one CTA per SM) whose CTAs loop over work items = two 128-query
+// tiles of one (b, h); 12 warps = 3 warpgroups; setmaxnreg moves registers from warpgroup 0 to the
+// softmax warpgroups:
+//   warp 0      TMA producer (tile layout: attn_common.cuh): each item's Q as soon as the previous
+//               item's last Q K^T completed, and per 128-key block a K tile and a V tile (3-stage
+//               ring that runs on across items);
+//   warps 2-3   the items' bias windows pd[h, ...] * log2(e) in shared memory (two copies, one
+//               shifted by an element, for aligned pair reads), double-buffered: the next item's
+//               window is filled while the current one is read (the first item's with the softmax
+//               warps' help); sequences too long for it fall back to per-block slabs the producer
+//               writes;
 //   warp 1      TMEM owner (512 columns) and the single-thread tcgen05.mma issuer:
 //               S_t = Q_t K^T (SS, K = DP) into TMEM, O_t += P_t V (TS: P read from TMEM, one
-//               N = DP instruction per 16 keys);
+//               N = DP instruction per 16 keys); the next item's first S tiles are issued right
+//               after the current item's last P V, so they run while O is written out;
 //   warps 4-7   softmax for query tile 0, warps 8-11 for tile 1 (one query row per thread,
 //               row = TMEM lane): S from TMEM -> bias add (paired fp32 FMAs) -> online softmax
 //               with the rescale of O skipped unless the running max grows by more than 2^8;
 //               exp2 on the SFU for 3/4 of the elements and on the FMA pipe (sm100.cuh) for
-//               1/4 -> P (bf16/f16) written back over S in TMEM -> at the end O / l to memory.
+//               1/4 -> P (bf16/f16) written back over S in TMEM -> at the item's end O / l to memory.
 // The two query tiles ping-pong so one tile's softmax overlaps the other tile's MMAs.
 // Every wait is bounded (watchdog.cuh); a stalled pipeline ends the CTA with an error word.
 #include <string.h>
@@ -40,14 +44,16 @@ using namespace sm100;
 using attn::kTileRows;
 
 constexpr int kBN = 128;            // keys per block
-constexpr int kQTiles = 2;          // query tiles per CTA
-constexpr int kThreads = 384;       // 3 warpgroups: {producer, MMA, -, -}, softmax tile 0, tile 1
-constexpr uint32_t kRegsCtl = 96;   // per-thread registers of warpgroup 0 after setmaxnreg
-constexpr uint32_t kRegsSm = 200;   // softmax warpgroups (launch 168 x 384 >= 128 x (96 + 2 x 200))
+constexpr int kQTiles = 2;          // query tiles per work item
+constexpr int kItemRows = kQTiles * kTileRows;   // queries per work item
+constexpr int kThreads = 384;       // 3 warpgroups: {producer, MMA, window fill}, softmax tile 0, tile 1
+constexpr uint32_t kRegsCtl = 112;  // per-thread registers of warpgroup 0 after setmaxnreg
+constexpr uint32_t kRegsSm = 192;   // softmax warpgroups (launch 168 x 384 >= 128 x (112 + 2 x 192))
 constexpr int kSlab = 384;          // floats per bias slab (2*128 + 128 - 1 = 383 used)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;   // log2 units: P <= 2^8 between rescales
-constexpr int kRowFillers = 320;           // warps 2-11 fill the resident bias window
+constexpr int kInitFillers = 320;          // warps 2-11 fill the first item's bias window
+constexpr int kBgFillers = 64;             // warps 2-3 fill the later items' windows
 
 template <int DP>
 struct FwdCfg {
@@ -57,9 +63,11 @@ struct FwdCfg {
   static constexpr uint32_t kKVOff = kQOff + kQTiles * kTile;
   static constexpr uint32_t kSlabOff = kKVOff + NS * 2 * kTile;
   static constexpr uint32_t kBarOff = kSlabOff + NS * kSlab * 4;
-  static constexpr int kNumBars = 1 + 2 * NS + 3 * kQTiles + 2;     // q_full, kv_full/empty, s/p/o, drain, row
+  // q_full, q_empty, kv_full/empty, s_ready/p_ready/o_final/o_free per tile, drain, row_init,
+  // row_full[2], row_free[2]
+  static constexpr int kNumBars = 2 + 2 * NS + 4 * kQTiles + 1 + 1 + 2 + 2;
   static constexpr uint32_t kMiscOff = kBarOff + kNumBars * 8;
-  static constexpr uint32_t kRowOff = kMiscOff + 16;                // resident bias row (runtime length)
+  static constexpr uint32_t kRowOff = (kMiscOff + 16 + 15) & ~15u;  // bias windows (runtime length)
   static constexpr uint32_t kSmem = kRowOff + 1024;                 // static part + alignment slack
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kSCol = 0;                              // S_t at t*128
@@ -75,33 +83,41 @@ struct FwdArgs {
   int B, S, H, D;
   float scale_log2;   // scale * log2(e)
   int n_kb;           // key blocks
+  int n_qp;           // query pairs (work items per head)
   uint32_t spin_limit;
+  int out32_v8;       // out32 is 32-byte aligned: 256-bit stores
 };
 
-// Resident bias row: pd[h, :] * log2(e) with kRowPad zeros before it and 128 after, so every
-// index a CTA forms (key - query + S - 1 for keys and queries up to 127 past S) stays inside.
-// Two copies, the second shifted by one element, so that every thread reads its 128 bias values
-// as 8-byte aligned pairs (copy 0 when its start index is even, copy 1 when odd).  Lane l of a warp
-// starts at B0 - l with B0 of the parity of S - 1; in a half-warp the copy-0 lanes then read 16
-// consecutive floats and the copy-1 lanes 16 more, shifted by the copy distance - 16 (S even) or
-// - 18 (S odd).  Spacing the copies 16 or 18 (mod 32) floats apart puts the two halves on disjoint
-// banks: one wavefront per half-warp.
+// Bias windows.  The bias of (query q, key k) is pd[h, k - q + S - 1].  A work item (queries q0 ..
+// q0 + 255, all keys) forms indices kRowPad + k - q + S - 1 in [w0 + 2, w0 + win_floats - 4] with
+// w0 = even(max(kRowPad + S - 1 - q0 - 257, 0)); the window stores them from w0 on, scaled by
+// log2(e), in two copies (the second shifted by one element) so that every thread reads its bias
+// values as 8-byte aligned pairs (copy 0 when its start index is even, copy 1 when odd).  Lane l
+// of a warp starts at B0 - l with B0 of the parity of S - 1: in a half-warp the copy-0 lanes read
+// 16 consecutive floats and the copy-1 lanes 16 more, shifted by the copy distance - 16 (S even) or
+// - 18 (S odd); copies 16 or 18 (mod 32) floats apart put the two halves on disjoint banks.  Two
+// windows (double buffer): the next item's window is filled while the current one is read.
 constexpr int kRowPad = 256;
-__host__ __device__ constexpr int64_t row_floats(int64_t S) {
-  return (2 * S - 1 + kRowPad + 128 + 31 - ((S & 1) ? 18 : 16)) / 32 * 32 + ((S & 1) ? 18 : 16);
+__host__ __device__ constexpr int64_t win_floats(int64_t S) {
+  return (((S + kBN - 1) / kBN) * kBN + 264 + 31 - ((S & 1) ? 18 : 16)) / 32 * 32 + ((S & 1) ? 18 : 16);
 }
-__host__ __device__ constexpr int64_t row_bytes(int64_t S) { return 2 * row_floats(S) * 4; }
+__host__ __device__ constexpr int64_t win_bytes(int64_t S) { return 4 * win_floats(S) * 4; }   // 2 windows x 2 copies
+__device__ __forceinline__ int win_start(int S, int q0) { return max(kRowPad + S - 1 - q0 - 257, 0) & ~1; }
 
-
-
-// dst[i] = src[i - pad] * log2(e) for i in [w0, w1), zero where i - pad is outside [0, len), by
-// kRowFillers cooperating threads.
-__device__ __forceinline__ void fill_row_window(float* dst, int w0, int w1, int pad, const float* __restrict__ src,
-                                                int len, int tid) {
-  const int s0 = max(w0 - pad, 0), s1 = min(w1 - pad, len);
-  attn::fill_row(dst + w0, w1 - w0, s0 + pad - w0, src + s0, max(s1 - s0, 0), kLog2e, tid, kRowFillers);
+// dst[i] = src[i + off] * log2(e) for i in [0, n), zero where i + off is outside [0, len), by nthr
+// cooperating threads.  The source range handed to fill_row is clipped to the window (fill_row
+// writes dst[pad + p] for every source element p it is given).
+__device__ __forceinline__ void fill_shifted(float* dst, int n, int off, const float* __restrict__ src, int len,
+                                             int tid, int nthr) {
+  if (off >= 0) attn::fill_row(dst, n, 0, src + min(off, len), min(max(len - off, 0), n), kLog2e, tid, nthr);
+  else attn::fill_row(dst, n, min(-off, n), src, min(len, max(n + off, 0)), kLog2e, tid, nthr);
 }
 
+// Persistent: one CTA per SM; work item it = (b*H + h) * n_qp + query pair, CTA c takes items
+// c, c + gridDim.x, ...  Across items the K/V ring, TMEM and the barriers carry on: Q of the next
+// item is loaded as soon as the last Q K^T of the current one has completed, its first S tiles are
+// computed while the softmax warps write the current item's output, and its bias window is filled
+// in the background by warps 2-3.
 template <int DP, bool F16, bool RES>
 __global__ void __launch_bounds__(kThreads, 1)
 relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
@@ -111,37 +127,49 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = bars + 1 + NS;
-  uint64_t* s_ready = bars + 1 + 2 * NS;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* kv_full = bars + 2;
+  uint64_t* kv_empty = kv_full + NS;
+  uint64_t* s_ready = kv_empty + NS;
   uint64_t* p_ready = s_ready + kQTiles;
   uint64_t* o_final = p_ready + kQTiles;
-  uint64_t* drain = o_final + kQTiles;
-  uint64_t* row_full = drain + 1;
-  float* row0 = reinterpret_cast<float*>(smem + C::kRowOff);
-  float* row1 = row0 + row_floats(a.S);
+  uint64_t* o_free = o_final + kQTiles;
+  uint64_t* drain = o_free + kQTiles;
+  uint64_t* row_init = drain + 1;
+  uint64_t* row_full = row_init + 1;   // [2]
+  uint64_t* row_free = row_full + 2;   // [2]
+  const int wf = (int)win_floats(a.S);
+  float* wins = reinterpret_cast<float*>(smem + C::kRowOff);   // window w, copy c at (2w + c) * wf
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
   float* slabs = reinterpret_cast<float*>(smem + C::kSlabOff);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
-  const int q0 = blockIdx.x * (kQTiles * kTileRows);
   const int n_kb = a.n_kb;
+  const int n_items = a.B * a.H * a.n_qp;
+  const int my_items = (int)blockIdx.x < n_items ? (n_items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  auto item_bh = [&](int k) { return ((int)blockIdx.x + k * (int)gridDim.x) / a.n_qp; };
+  auto item_q0 = [&](int k) { return (((int)blockIdx.x + k * (int)gridDim.x) % a.n_qp) * kItemRows; };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int s = 0; s < NS; ++s) {
       mbar_init(&kv_full[s], RES ? 1 : 2);   // TMA expect_tx arrival (+ bias-slab arrival)
-      mbar_init(&kv_empty[s], 1);    // tcgen05.commit
+      mbar_init(&kv_empty[s], 1);            // tcgen05.commit
     }
     for (int t = 0; t < kQTiles; ++t) {
       mbar_init(&s_ready[t], 1);
       mbar_init(&p_ready[t], 128);
       mbar_init(&o_final[t], 1);
+      mbar_init(&o_free[t], 128);
     }
     mbar_init(drain, 1);
-    mbar_init(row_full, kRowFillers);
+    mbar_init(row_init, kInitFillers);
+    for (int w = 0; w < 2; ++w) {
+      mbar_init(&row_full[w], kBgFillers);
+      mbar_init(&row_free[w], 2 * 128);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -154,19 +182,15 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // Resident bias window (RES), filled by warps 2-11 (the softmax warps are idle until their first
-  // S tile): only the indices this CTA forms, kRowPad + key - query + S - 1 for its 256 queries and
-  // all keys, plus one on each side for the shifted copy.
-  auto fill_window = [&]() {
+
+  // The bias window of item k into window k & 1 (RES), by `nthr` threads.
+  auto fill_window = [&](int k, int tid, int nthr) {
     const int two_s = 2 * a.S - 1;
-    const float* pdh = a.pd + (size_t)h * two_s;
-    const int n = (int)row_floats(a.S);
-    const int tid = threadIdx.x - 64;
-    const int w0 = max(kRowPad + a.S - 1 - (q0 + kQTiles * kTileRows - 1) - 1, 0);
-    const int w1 = min(kRowPad + a.S - 1 - q0 + n_kb * kBN + 1, n);
-    fill_row_window(row0, w0, w1, kRowPad, pdh, two_s, tid);
-    fill_row_window(row1, w0, w1, kRowPad - 1, pdh, two_s, tid);   // row1[i] = row0[i + 1]
-    mbar_arrive(row_full);
+    const float* pdh = a.pd + (size_t)(item_bh(k) % a.H) * two_s;
+    const int w0 = win_start(a.S, item_q0(k));
+    float* c0 = wins + (size_t)(2 * (k & 1)) * wf;
+    fill_shifted(c0, wf, w0 - kRowPad, pdh, two_s, tid, nthr);
+    fill_shifted(c0 + wf, wf, w0 - kRowPad + 1, pdh, two_s, tid, nthr);   // copy 1: c1[i] = c0[i + 1]
   };
   // Each role runs entirely inside the branch that sets its register budget, so ptxas compiles
   // it against that budget.
@@ -174,40 +198,68 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
     regs_dec<kRegsCtl>();
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, kQTiles * C::kTile);
-      for (int t = 0; t < kQTiles; ++t)
-        attn::load_tile<DP>(smem + C::kQOff + t * C::kTile, &tmap, q_full, h, q0 + t * kTileRows, b);
-    }
-    const int two_s = 2 * a.S - 1;
-    const float* pdh = a.pd + (size_t)h * two_s;
-
-    for (int j = 0; j < n_kb; ++j) {
-      const int s = j % NS;
-      if (j >= NS && !mbar_wait_bounded(&kv_empty[s], ((j / NS) + 1) & 1, abort_flag, a.spin_limit)) {
+    int g = 0;   // global key-block counter (K/V ring position)
+    for (int k = 0; k < my_items; ++k) {
+      const int bh = item_bh(k), b = bh / a.H, h = bh % a.H, q0 = item_q0(k);
+      if (k > 0 && !mbar_wait_bounded(q_empty, (k - 1) & 1, abort_flag, a.spin_limit)) {
         watchdog_fire(kWdFwdLoad);
         break;
       }
-      uint8_t* kt = smem + C::kKVOff + (2 * s) * C::kTile;
       if (lane == 0) {
-        mbar_arrive_expect_tx(&kv_full[s], 2 * C::kTile);
-        attn::load_tile<DP>(kt, &tmap, &kv_full[s], a.H + h, j * kBN, b);
-        attn::load_tile<DP>(kt + C::kTile, &tmap, &kv_full[s], 2 * a.H + h, j * kBN, b);
+        mbar_arrive_expect_tx(q_full, kQTiles * C::kTile);
+        for (int t = 0; t < kQTiles; ++t)
+          attn::load_tile<DP>(smem + C::kQOff + t * C::kTile, &tmap, q_full, h, q0 + t * kTileRows, b);
       }
-      if constexpr (RES) continue;
-      // bias slab: slab[idx] = pd[h, j*128 - q0 - 255 + idx + S - 1] * log2e, zero outside the table
-      float* slab = slabs + s * kSlab;
-      const int base = j * kBN - q0 - (kQTiles * kTileRows - 1) + a.S - 1;
-      for (int idx = lane; idx < kSlab; idx += 32) {
-        const int pos = base + idx;
-        slab[idx] = (pos >= 0 && pos < two_s) ? __ldg(pdh + pos) * kLog2e : 0.f;
+      const int two_s = 2 * a.S - 1;
+      const float* pdh = a.pd + (size_t)h * two_s;
+      bool ok = true;
+      for (int j = 0; j < n_kb; ++j, ++g) {
+        const int s = g % NS;
+        if (g >= NS && !mbar_wait_bounded(&kv_empty[s], ((g / NS) + 1) & 1, abort_flag, a.spin_limit)) {
+          ok = false;
+          break;
+        }
+        uint8_t* kt = smem + C::kKVOff + (2 * s) * C::kTile;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&kv_full[s], 2 * C::kTile);
+          attn::load_tile<DP>(kt, &tmap, &kv_full[s], a.H + h, j * kBN, b);
+          attn::load_tile<DP>(kt + C::kTile, &tmap, &kv_full[s], 2 * a.H + h, j * kBN, b);
+        }
+        if constexpr (RES) continue;
+        // bias slab: slab[idx] = pd[h, j*128 - q0 - 255 + idx + S - 1] * log2e, zero outside the table
+        float* slab = slabs + s * kSlab;
+        const int base = j * kBN - q0 - (kItemRows - 1) + a.S - 1;
+        for (int idx = lane; idx < kSlab; idx += 32) {
+          const int pos = base + idx;
+          slab[idx] = (pos >= 0 && pos < two_s) ? __ldg(pdh + pos) * kLog2e : 0.f;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&kv_full[s]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&kv_full[s]);
+      if (!ok) {
+        watchdog_fire(kWdFwdLoad);
+        break;
+      }
     }
   } else if (warp == 2 || warp == 3) {
-    // ------------------------------------------------------------ resident bias window (RES)
-    if constexpr (RES) fill_window();
+    // ------------------------------------------------------------ bias windows (RES)
+    if constexpr (RES) {
+      const int tid = threadIdx.x - 64;
+      if (my_items > 0) {
+        fill_window(0, tid, kInitFillers);
+        mbar_arrive(row_init);
+      }
+      for (int k = 1; k < my_items; ++k) {
+        // window k & 1 is free once every softmax thread has finished item k - 2
+        if (k >= 2 && !__all_sync(0xffffffffu, mbar_wait_bounded(&row_free[k & 1], ((k - 2) >> 1) & 1, abort_flag,
+                                                                   a.spin_limit))) {
+          watchdog_fire(kWdFwdLoad);
+          break;
+        }
+        fill_window(k, tid, kBgFillers);
+        mbar_arrive(&row_full[k & 1]);
+      }
+    }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -221,56 +273,89 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
       const uint64_t v_desc0 = attn::mnmajor_base(smem_u32(smem + C::kKVOff + C::kTile));
       constexpr uint64_t kStageStep = (2 * C::kTile) >> 4;
       constexpr uint64_t kQTileStep = C::kTile >> 4;
-      bool ok = mbar_wait_bounded(q_full, 0, abort_flag, a.spin_limit) &&
-                mbar_wait_bounded(&kv_full[0], 0, abort_flag, a.spin_limit);
-      auto issue_qk = [&](int t, int j) {
+      auto issue_qk = [&](int t, int g) {
         const uint64_t qd = q_desc + (uint64_t)t * kQTileStep;
-        const uint64_t kd = k_desc0 + (uint64_t)(j % NS) * kStageStep;
+        const uint64_t kd = k_desc0 + (uint64_t)(g % NS) * kStageStep;
         const uint32_t d = tmem + C::kSCol + t * kBN;
 #pragma unroll
         for (int kk = 0; kk < DP / 16; ++kk)
           mma_ss(d, qd + kk * attn::kKSliceStep, kd + kk * attn::kKSliceStep, id_qk, kk > 0 ? 1u : 0u);
       };
-      auto issue_pv = [&](int t, int j) {
-        const uint64_t vd = v_desc0 + (uint64_t)(j % NS) * kStageStep;
+      auto issue_pv = [&](int t, int g, bool first) {
+        const uint64_t vd = v_desc0 + (uint64_t)(g % NS) * kStageStep;
         const uint32_t p_tmem = tmem + C::kSCol + t * kBN;   // P: 2 x 16-bit per column
         const uint32_t d = tmem + C::kOCol + t * DP;
-        const uint32_t acc0 = j > 0 ? 1u : 0u;
+        const uint32_t acc0 = first ? 0u : 1u;
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk)
           mma_ts(d, p_tmem + kk * 8, vd + kk * attn::kKRowStep, id_pv, kk > 0 ? 1u : acc0);
       };
+      bool ok = my_items > 0 && mbar_wait_bounded(q_full, 0, abort_flag, a.spin_limit) &&
+                mbar_wait_bounded(&kv_full[0], 0, abort_flag, a.spin_limit);
       if (ok) {
         tc_fence_after();
         for (int t = 0; t < kQTiles; ++t) {
           issue_qk(t, 0);
           mma_commit(&s_ready[t]);
         }
-        for (int j = 0; j < n_kb && ok; ++j) {
-          const bool has_next = j + 1 < n_kb;
-          if (has_next && !mbar_wait_bounded(&kv_full[(j + 1) % NS], ((j + 1) / NS) & 1, abort_flag, a.spin_limit)) {
-            ok = false;
-            break;
-          }
-          for (int t = 0; t < kQTiles; ++t) {
-            if (!mbar_wait_bounded(&p_ready[t], j & 1, abort_flag, a.spin_limit)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_pv(t, j);
-            if (has_next) {
-              issue_qk(t, j + 1);
+        if (n_kb == 1) mma_commit(q_empty);   // item 0's only Q K^T is issued
+      }
+      int g = 0;
+      for (int k = 0; k < my_items && ok; ++k) {
+        for (int j = 0; j < n_kb && ok; ++j, ++g) {
+          // the next block: (k, j + 1) or the next item's first
+          const bool last_j = j + 1 == n_kb;
+          const bool has_next = !last_j || k + 1 < my_items;
+          auto wait_next = [&]() {   // K/V of block g + 1 (and, for a new item, its Q) landed
+            return mbar_wait_bounded(&kv_full[(g + 1) % NS], ((g + 1) / NS) & 1, abort_flag, a.spin_limit) &&
+                   (!last_j || mbar_wait_bounded(q_full, (k + 1) & 1, abort_flag, a.spin_limit));
+          };
+          if (!last_j) {
+            // inside an item: P V then the next S, tile by tile
+            for (int t = 0; t < kQTiles; ++t) {
+              if (!mbar_wait_bounded(&p_ready[t], g & 1, abort_flag, a.spin_limit) ||
+                  (j == 0 && k > 0 && !mbar_wait_bounded(&o_free[t], (k - 1) & 1, abort_flag, a.spin_limit)) ||
+                  (t == 0 && !wait_next())) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_pv(t, g, j == 0);
+              issue_qk(t, g + 1);
               mma_commit(&s_ready[t]);
-            } else {
+            }
+          } else {
+            // an item's last block: both P V first (its output is written out while the next
+            // item's Q and first K/V arrive), then the next item's first S tiles
+            for (int t = 0; t < kQTiles; ++t) {
+              if (!mbar_wait_bounded(&p_ready[t], g & 1, abort_flag, a.spin_limit) ||
+                  (j == 0 && k > 0 && !mbar_wait_bounded(&o_free[t], (k - 1) & 1, abort_flag, a.spin_limit))) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_pv(t, g, j == 0);
               mma_commit(&o_final[t]);
+            }
+            if (ok && has_next) {
+              if (!wait_next()) {
+                ok = false;
+              } else {
+                tc_fence_after();
+                for (int t = 0; t < kQTiles; ++t) {
+                  issue_qk(t, g + 1);
+                  mma_commit(&s_ready[t]);
+                }
+              }
             }
           }
           if (!ok) break;
-          mma_commit(&kv_empty[j % NS]);
+          // the Q K^T just issued was the last one of its item: its Q may be replaced
+          if (has_next && (last_j ? n_kb == 1 : j + 2 == n_kb)) mma_commit(q_empty);
+          mma_commit(&kv_empty[g % NS]);
         }
       }
-      if (!ok) watchdog_fire(kWdFwdMma);
+      if (!ok && my_items > 0) watchdog_fire(kWdFwdMma);
       // Drain: every MMA issued above has completed before TMEM is released.
       mma_commit(drain);
       for (uint32_t i = 0; i < a.spin_limit && !mbar_try_wait(drain, 0); ++i) {
@@ -279,157 +364,192 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
   }
   } else {
     regs_inc<kRegsSm>();
-    if constexpr (RES) fill_window();
+    if constexpr (RES) {
+      if (my_items > 0) {
+        fill_window(0, threadIdx.x - 64, kInitFillers);
+        mbar_arrive(row_init);
+      }
+    }
     // ------------------------------------------------------------ softmax (warps 4..11)
     const int t = (warp - 4) / 4;                       // query tile
     const int quarter = warp % 4;                       // TMEM lane quarter of this warp
     const int r = quarter * 32 + lane;                  // row within the tile
-    const int q = q0 + t * kTileRows + r;               // query index within the sequence
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
     const uint32_t s_tmem = tmem + lane_addr + C::kSCol + t * kBN;
     const uint32_t o_tmem = tmem + lane_addr + C::kOCol + t * DP;
     const int slab_base = (kQTiles - 1 - t) * kTileRows + (kTileRows - 1) - r;   // slab[slab_base + c]
-    // resident row: bias(q, key j*128 + c) = row0[bidx + c], bidx = kRowPad + j*128 - q + S - 1
-    const int bidx0 = kRowPad - q + a.S - 1;
-    const float* bias_q = (bidx0 & 1) ? row1 + bidx0 - 1 : row0 + bidx0;   // 8-byte aligned pairs
     const uint64_t scale2 = f2_pack(a.scale_log2, a.scale_log2);
-    float m_run = -INFINITY, l_run = 0.f;
-    bool ok = !RES || __all_sync(0xffffffffu, mbar_wait_bounded(row_full, 0, abort_flag, a.spin_limit));
-    for (int j = 0; j < n_kb && ok; ++j) {
-      const int s = j % NS;
-      const bool w_ok = mbar_wait_bounded(&s_ready[t], j & 1, abort_flag, a.spin_limit) &&
-                        (RES || mbar_wait_bounded(&kv_full[s], (j / NS) & 1, abort_flag, a.spin_limit));
-      if (!__all_sync(0xffffffffu, w_ok)) {   // warp-uniform: TMEM loads/stores are warp-collective
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t u[kBN];
-#pragma unroll
-      for (int c = 0; c < kBN; c += 32) tmem_ld32(s_tmem + c, u + c);
-      tmem_wait_ld();
-      // v = s * scale * log2(e) + bias * log2(e), two columns per instruction
-      uint64_t v2[kBN / 2];
+    bool ok = true;
+    int g = 0;
+    for (int k = 0; k < my_items && ok; ++k) {
+      const int bh = item_bh(k), b = bh / a.H, q0 = item_q0(k);
+      const int q = q0 + t * kTileRows + r;             // query index within the sequence
+      // window: bias(q, key j*128 + c) = win[bidx + c], bidx = kRowPad + j*128 - q + S - 1 - w0
+      const float* bias_q = nullptr;
       if constexpr (RES) {
-        const uint64_t* bp = reinterpret_cast<const uint64_t*>(bias_q + j * kBN);
-#pragma unroll
-        for (int i = 0; i < kBN / 2; ++i)
-          v2[i] = f2_fma(f2_pack(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1])), scale2, bp[i]);
-      } else {
-        const float* slab = slabs + s * kSlab + slab_base;
-#pragma unroll
-        for (int i = 0; i < kBN / 2; ++i)
-          v2[i] = f2_fma(f2_pack(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1])), scale2,
-                         f2_pack(slab[2 * i], slab[2 * i + 1]));
+        const bool w_ok = k == 0 ? mbar_wait_bounded(row_init, 0, abort_flag, a.spin_limit)
+                                 : mbar_wait_bounded(&row_full[k & 1], ((k - 1) >> 1) & 1, abort_flag, a.spin_limit);
+        if (!__all_sync(0xffffffffu, w_ok)) {
+          ok = false;
+          break;
+        }
+        const int bidx0 = kRowPad - q + a.S - 1 - win_start(a.S, q0);
+        const float* c0 = wins + (size_t)(2 * (k & 1)) * wf;
+        bias_q = (bidx0 & 1) ? c0 + wf + bidx0 - 1 : c0 + bidx0;   // 8-byte aligned pairs
       }
-      const int valid = a.S - j * kBN;                  // keys of this block inside the sequence
-      if (valid < kBN) {                                // only the last block of a ragged sequence
+      float m_run = -INFINITY, l_run = 0.f;
+      for (int j = 0; j < n_kb; ++j, ++g) {
+        const int s = g % NS;
+        const bool w_ok = mbar_wait_bounded(&s_ready[t], g & 1, abort_flag, a.spin_limit) &&
+                          (RES || mbar_wait_bounded(&kv_full[s], (g / NS) & 1, abort_flag, a.spin_limit));
+        if (!__all_sync(0xffffffffu, w_ok)) {   // warp-uniform: TMEM loads/stores are warp-collective
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t u[kBN];
+#pragma unroll
+        for (int c = 0; c < kBN; c += 32) tmem_ld32(s_tmem + c, u + c);
+        tmem_wait_ld();
+        // v = s * scale * log2(e) + bias * log2(e), two columns per instruction
+        uint64_t v2[kBN / 2];
+        if constexpr (RES) {
+          const uint64_t* bp = reinterpret_cast<const uint64_t*>(bias_q + j * kBN);
+#pragma unroll
+          for (int i = 0; i < kBN / 2; ++i)
+            v2[i] = f2_fma(f2_pack(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1])), scale2, bp[i]);
+        } else {
+          const float* slab = slabs + s * kSlab + slab_base;
+#pragma unroll
+          for (int i = 0; i < kBN / 2; ++i)
+            v2[i] = f2_fma(f2_pack(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1])), scale2,
+                           f2_pack(slab[2 * i], slab[2 * i + 1]));
+        }
+        const int valid = a.S - j * kBN;                  // keys of this block inside the sequence
+        if (valid < kBN) {                                // only the last block of a ragged sequence
+#pragma unroll
+          for (int i = 0; i < kBN / 2; ++i) {
+            float lo, hi;
+            f2_unpack(v2[i], lo, hi);
+            v2[i] = f2_pack(2 * i < valid ? lo : -INFINITY, 2 * i + 1 < valid ? hi : -INFINITY);
+          }
+        }
+        // row max: 3-input max, 4 independent chains
+        float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
         for (int i = 0; i < kBN / 2; ++i) {
           float lo, hi;
           f2_unpack(v2[i], lo, hi);
-          v2[i] = f2_pack(2 * i < valid ? lo : -INFINITY, 2 * i + 1 < valid ? hi : -INFINITY);
+          mxa[i % 4] = max3(mxa[i % 4], lo, hi);
         }
-      }
-      // row max: 3-input max, 4 independent chains
-      float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-      for (int i = 0; i < kBN / 2; ++i) {
-        float lo, hi;
-        f2_unpack(v2[i], lo, hi);
-        mxa[i % 4] = max3(mxa[i % 4], lo, hi);
-      }
-      const float mx = fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3]));
-      const float m_new = fmaxf(m_run, mx);
-      const bool need = m_new - m_run > kRescaleThreshold;   // true on the first block (m_run = -inf)
-      float alpha = 1.f, m_use = m_run;
-      const bool warp_rescale = __any_sync(0xffffffffu, need);
-      if (warp_rescale) {
-        m_use = m_new;
-        alpha = ex2_approx(m_run - m_new);              // 0 on the first block
-      }
-      // p = 2^(v - m): three of every four pairs on the SFU, one on the FMA pipe (balances the
-      // SFU against the issue slots); row sum in 4 paired chains; P packed to 16-bit pairs
-      const uint64_t negm2 = f2_pack(-m_use, -m_use);
-      uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
-      uint32_t pk[kBN / 2];
-#pragma unroll
-      for (int i = 0; i < kBN / 2; ++i) {
-        float x0, x1, p0, p1;
-        f2_unpack(f2_add(v2[i], negm2), x0, x1);
-        if (i % 4 == 3) {
-          exp2_poly3_x2(x0, x1, p0, p1);
-        } else {
-          p0 = ex2_approx(x0);
-          p1 = ex2_approx(x1);
+        const float mx = fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3]));
+        const float m_new = fmaxf(m_run, mx);
+        const bool need = m_new - m_run > kRescaleThreshold;   // true on the first block (m_run = -inf)
+        float alpha = 1.f, m_use = m_run;
+        const bool warp_rescale = __any_sync(0xffffffffu, need);
+        if (warp_rescale) {
+          m_use = m_new;
+          alpha = ex2_approx(m_run - m_new);              // 0 on the first block
         }
-        acc2[i % 4] = f2_add(acc2[i % 4], f2_pack(p0, p1));
-        pk[i] = F16 ? pack_f16x2(p0, p1) : pack_bf16x2(p0, p1);
-      }
-      float sum_lo, sum_hi;
-      f2_unpack(f2_add(f2_add(acc2[0], acc2[1]), f2_add(acc2[2], acc2[3])), sum_lo, sum_hi);
-      const float sum = sum_lo + sum_hi;
-      l_run = l_run * alpha + sum;
-      m_run = m_use;
-      tmem_st32(s_tmem, pk);
-      tmem_st32(s_tmem + 32, pk + 32);
-      if (warp_rescale && j > 0) {
-        // O_t holds the sum through block j-1 (PV(t, j-1) completed before S_t(j) was ready).
+        // p = 2^(v - m): three of every four pairs on the SFU, one on the FMA pipe (balances the
+        // SFU against the issue slots); row sum in 4 paired chains; P packed to 16-bit pairs
+        const uint64_t negm2 = f2_pack(-m_use, -m_use);
+        uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
+        uint32_t pk[kBN / 2];
 #pragma unroll
-        for (int c = 0; c < DP; c += 16) {
-          uint32_t ov[16];
-          tmem_ld16(o_tmem + c, ov);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 16; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-          tmem_st16(o_tmem + c, ov);
+        for (int i = 0; i < kBN / 2; ++i) {
+          float x0, x1, p0, p1;
+          f2_unpack(f2_add(v2[i], negm2), x0, x1);
+          if (i % 4 == 3) {
+            exp2_poly3_x2(x0, x1, p0, p1);
+          } else {
+            p0 = ex2_approx(x0);
+            p1 = ex2_approx(x1);
+          }
+          acc2[i % 4] = f2_add(acc2[i % 4], f2_pack(p0, p1));
+          pk[i] = F16 ? pack_f16x2(p0, p1) : pack_bf16x2(p0, p1);
         }
+        float sum_lo, sum_hi;
+        f2_unpack(f2_add(f2_add(acc2[0], acc2[1]), f2_add(acc2[2], acc2[3])), sum_lo, sum_hi);
+        const float sum = sum_lo + sum_hi;
+        l_run = l_run * alpha + sum;
+        m_run = m_use;
+        tmem_st32(s_tmem, pk);
+        tmem_st32(s_tmem + 32, pk + 32);
+        if (warp_rescale && j > 0) {
+          // O_t holds the sum through block j-1 (PV(t, j-1) completed before S_t(j) was ready).
+#pragma unroll
+          for (int c = 0; c < DP; c += 16) {
+            uint32_t ov[16];
+            tmem_ld16(o_tmem + c, ov);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+            tmem_st16(o_tmem + c, ov);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_ready[t]);
       }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&p_ready[t]);
-    }
-    if (ok && !__all_sync(0xffffffffu, mbar_wait_bounded(&o_final[t], 0, abort_flag, a.spin_limit))) ok = false;
-    if (!ok) {
-      watchdog_fire(kWdFwdSoftmax);
-    } else {
+      if (!ok) break;
+      if constexpr (RES) mbar_arrive(&row_free[k & 1]);   // this item's window is no longer read
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&o_final[t], k & 1, abort_flag, a.spin_limit))) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       // All lanes run the warp-collective TMEM loads; rows past the sequence end skip the stores.
       const bool row_ok = q < a.S;
       const float inv_l = 1.0f / l_run;
       const size_t row = (size_t)b * a.S + (row_ok ? q : 0);
       const size_t ld = (size_t)a.H * a.D;
-      float* o32 = a.out32 + row * ld + (size_t)h * a.D;
+      float* o32 = a.out32 + row * ld + (size_t)(bh % a.H) * a.D;
       using T = typename std::conditional<F16, __half, __nv_bfloat16>::type;
-      T* o16 = reinterpret_cast<T*>(a.out) + row * ld + (size_t)h * a.D;
+      T* o16 = reinterpret_cast<T*>(a.out) + row * ld + (size_t)(bh % a.H) * a.D;
+      // O in column groups of up to 96 (one group for DP <= 96): a group is read from TMEM, then
+      // stored; O_t is released for the next item's first P V once its last group is read.
+      constexpr int kGrp = DP <= 96 ? DP : DP / 2;
 #pragma unroll
-      for (int c = 0; c < DP; c += 16) {
-        uint32_t ov[16];
-        tmem_ld16(o_tmem + c, ov);
-        tmem_wait_ld();
-        float f[16];
+      for (int c0 = 0; c0 < DP; c0 += kGrp) {
+        float ofin[kGrp];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) f[e] = __uint_as_float(ov[e]) * inv_l;
+        for (int c = 0; c < kGrp; c += 16) {
+          uint32_t ov[16];
+          tmem_ld16(o_tmem + c0 + c, ov);
+          tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 16; e += 8) {
-          if (row_ok && c + e < a.D) {   // D is a multiple of 8: whole 8-column groups are in or out
-            float4* d32 = reinterpret_cast<float4*>(o32 + c + e);
-            d32[0] = make_float4(f[e], f[e + 1], f[e + 2], f[e + 3]);
-            d32[1] = make_float4(f[e + 4], f[e + 5], f[e + 6], f[e + 7]);
-            uint4 pk;
-            if (F16) {
-              pk = make_uint4(pack_f16x2(f[e], f[e + 1]), pack_f16x2(f[e + 2], f[e + 3]),
-                              pack_f16x2(f[e + 4], f[e + 5]), pack_f16x2(f[e + 6], f[e + 7]));
+          for (int e = 0; e < 16; ++e) ofin[c + e] = __uint_as_float(ov[e]) * inv_l;
+        }
+        if (c0 + kGrp == DP) {   // O_t has been read: the next item's first P V may overwrite it
+          tc_fence_before();
+          mbar_arrive(&o_free[t]);
+        }
+#pragma unroll
+        for (int c = 0; c < kGrp; c += 8) {
+          if (row_ok && c0 + c < a.D) {   // D is a multiple of 8: whole 8-column groups are in or out
+            const float* f = ofin + c;
+            float* d32p = o32 + c0 + c;
+            if (a.out32_v8) {   // one 32-byte store per 8 columns (each row's chunk is its own line)
+              asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(d32p), "f"(f[0]),
+                           "f"(f[1]), "f"(f[2]), "f"(f[3]), "f"(f[4]), "f"(f[5]), "f"(f[6]), "f"(f[7])
+                           : "memory");
             } else {
-              pk = make_uint4(pack_bf16x2(f[e], f[e + 1]), pack_bf16x2(f[e + 2], f[e + 3]),
-                              pack_bf16x2(f[e + 4], f[e + 5]), pack_bf16x2(f[e + 6], f[e + 7]));
+              float4* d32 = reinterpret_cast<float4*>(d32p);
+              d32[0] = make_float4(f[0], f[1], f[2], f[3]);
+              d32[1] = make_float4(f[4], f[5], f[6], f[7]);
             }
-            *reinterpret_cast<uint4*>(o16 + c + e) = pk;
+            const uint4 pk = F16 ? make_uint4(pack_f16x2(f[0], f[1]), pack_f16x2(f[2], f[3]),
+                                              pack_f16x2(f[4], f[5]), pack_f16x2(f[6], f[7]))
+                                 : make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                                              pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+            *reinterpret_cast<uint4*>(o16 + c0 + c) = pk;
           }
         }
       }
       if (row_ok) a.lse[(size_t)bh * a.S + q] = m_run + __log2f(l_run);
     }
+    if (!ok) watchdog_fire(kWdFwdSoftmax);
   }
 
   tc_fence_before();
@@ -443,12 +563,13 @@ constexpr size_t kMaxSmem = 232448;   // 227 KB per CTA on sm_100
 template <int DP, bool F16>
 int launch_fwd(const CUtensorMap& tmap, const FwdArgs& a, cudaStream_t stream) {
   using C = FwdCfg<DP>;
-  const size_t res_smem = C::kSmem + (size_t)row_bytes(a.S);
+  const size_t res_smem = C::kSmem + (size_t)win_bytes(a.S);
   const bool res = res_smem <= kMaxSmem;
   auto kern = res ? relpos_fwd_kernel<DP, F16, true> : relpos_fwd_kernel<DP, F16, false>;
   const size_t smem = res ? res_smem : C::kSmem;
   KRSI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  dim3 grid((a.S + kQTiles * kTileRows - 1) / (kQTiles * kTileRows), a.B * a.H);
+  const int64_t items = (int64_t)a.B * a.H * a.n_qp;   // persistent: at most one CTA per SM
+  const int grid = (int)(items < device_sm_count() ? items : device_sm_count());
   kern<<<grid, kThreads, smem, stream>>>(tmap, a);
   KRSI_LAUNCH_CHECK();
   return KRSI_OK;
@@ -498,7 +619,9 @@ extern "C" int krsi_relpos_attn_fwd(const void* qkv, int64_t qkv_row_stride, con
   if (S > (1 << 24) || B * H > 65535) return KRSI_ERR_UNSUPPORTED;
   CUtensorMap tmap;
   if (!attn::make_head_map(&tmap, qkv, qkv_row_stride, B, S, 3 * H, D, dtype == KRSI_F16)) return KRSI_ERR_CUDA;
+  if (B * H * ((S + kItemRows - 1) / kItemRows) > INT32_MAX) return KRSI_ERR_UNSUPPORTED;
   FwdArgs a{pd, out, out32, lse, (int)B, (int)S, (int)H, (int)D, scale * 1.4426950408889634f,
-            (int)((S + kBN - 1) / kBN), kSpinLimit};
+            (int)((S + kBN - 1) / kBN), (int)((S + kItemRows - 1) / kItemRows), kSpinLimit,
+            (reinterpret_cast<uintptr_t>(out32) & 31) == 0 ? 1 : 0};
   return dtype == KRSI_F16 ? dispatch_dp<true>(DP, tmap, a, stream) : dispatch_dp<false>(DP, tmap, a, stream);
 }

@@ -41,6 +41,8 @@ def attn_fwd_check(B, S, H, D, dtype=torch.bfloat16, seed=0, tol=1e-2):
     (2, 520, 2, 32),
     (1, 384, 2, 128),
     (1, 200, 1, 96),
+    (3, 700, 5, 72),     # persistent grid: work items not a multiple of the CTAs, ragged pairs
+    (1, 4608, 1, 72),    # windows too long for shared memory: per-block bias slabs
 ])
 def test_fwd_small_shapes(B, S, H, D):
     attn_fwd_check(B, S, H, D, seed=B * 1000 + S + D)
