@@ -1,7 +1,8 @@
 """The 28-layer pre-norm block stack of BASELINE config 5, built on the drop-in library ops.
 
-Each layer:  x -> RMSNorm -> fused q|k|v GEMM -> relpos attention (H heads of D) -> out GEMM -> +x
-                -> RMSNorm -> merged gate|value GEMM (d -> 2F) -> GEGLU -> down GEMM (F -> d) -> +x
+Each layer:  x -> RMSNorm -> fused q|k|v GEMM -> relpos attention (H heads of D) -> out GEMM + x
+                -> RMSNorm -> merged gate|value GEMM (d -> 2F) -> GEGLU -> down GEMM (F -> d) + x
+(the residual adds ride in the out and down GEMMs: addmm with beta = 1)
 The attention, RMSNorm and GEGLU calls are the kernel-rsi library functions (relpos_attention(),
 rmsnorm(), geglu(), with the reference's signatures); the GEMMs are torch matmuls (cuBLAS).  loss =
 mean(out.float()^2).  Weights are bf16 ~ N(0, 0.02) (RMSNorm weights 1 + N(0, 0.02)), the per-layer
@@ -66,10 +67,10 @@ class Layer(nn.Module):
         h = ops.rmsnorm(x2, self.norm1, cfg.eps)
         qkv = h @ self.wqkv.t()
         a = ops.relpos_attention(qkv, self.pd, B, L, cfg.heads, cfg.head_dim, 1.0 / math.sqrt(cfg.head_dim))
-        x2 = x2 + a @ self.wo.t()
+        x2 = torch.addmm(x2, a, self.wo.t())        # residual add inside the GEMM (beta = 1)
         h = ops.rmsnorm(x2, self.norm2, cfg.eps)
         g = ops.geglu(h @ self.wi.t())
-        x2 = x2 + g @ self.wo2.t()
+        x2 = torch.addmm(x2, g, self.wo2.t())
         return x2.reshape(B, L, d)
 
 
