@@ -280,7 +280,7 @@ class AttnWorkload(OpWorkload):
     def in_bytes(self):
         return self.B * self.S * self.H * self.D * 2 * (3 if self.fwd_only else 4)
 
-    launches_per_step = 5   # fwd; bwd prep, main, dq, dpd
+    launches_per_step = 6   # fwd; bwd prep, main, dq, dpd_diag, dpd
     kernel_key = "relpos_bwd_main_kernel"
 
     def config(self):
@@ -356,7 +356,7 @@ class AttnWorkload(OpWorkload):
         if self.fwd_only:
             t, flop, key = statistics.median(fwd), self.work, "relpos_fwd_kernel"
         else:
-            t, flop, key = statistics.median(bwd), 8 * self.B * self.H * self.S ** 2 * self.D, "relpos_bwd (4 kernels)"
+            t, flop, key = statistics.median(bwd), 8 * self.B * self.H * self.S ** 2 * self.D, "relpos_bwd (5 kernels)"
         ach = flop / (t / 1e3) / 1e12
         return {"bound": "tensor", "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": ach / pk["bf16_tflops"], "traffic": ncu_traffic(key), "kernel": key,
@@ -457,7 +457,7 @@ class BlockWorkload:
         self.cfg = hb.BlockConfig()
         self.tokens_per_step = self.GLOBAL_B * self.cfg.seq // world      # this rank's tokens
         self.work = self.cfg.flops_per_token() * self.GLOBAL_B * self.cfg.seq
-        self.launches_per_step = self.cfg.layers * 13   # rmsnorm 2x(1+2), attn 1+4, geglu 1+1
+        self.launches_per_step = self.cfg.layers * 14   # rmsnorm 2x(1+2), attn 1+5, geglu 1+1
 
     def config(self):
         c = self.cfg
@@ -510,7 +510,7 @@ class BlockWorkload:
         self._attn = {"attn_ms_per_step": t, "attn_fwd_ms_per_step": statistics.median(fwd),
                       "attn_share_of_step": t / kms if kms else None}
         return {"bound": "tensor", "achieved": ach, "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
-                "frac": ach / pk["bf16_tflops_sustained"], "traffic": ncu_traffic("relpos_bwd_main_kernel"),
+                "frac": ach / pk["bf16_tflops_sustained"], "traffic": ncu_traffic(self.kernel_key),
                 "kernel": self.kernel_key, "peak_source": pk["source"] + " (sustained bf16 cuBLAS: timed inside a long step)"}
 
     def extra(self):
