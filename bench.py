@@ -131,7 +131,7 @@ def cpu_info() -> str:
 
 # ---------------------------------------------------------------- workloads
 # Each workload exposes: metric, unit, work_per_step (bytes or FLOP), setup(dev), step(),
-# e2e_step() (host buffers in, result read back), launches_per_step, dominant kernel timing,
+# e2e_loop(dev, n) (host buffers in, results read back), launches_per_step, dominant kernel timing,
 # and a CPU sample for the baseline.
 
 class OpWorkload:
@@ -149,7 +149,7 @@ class OpWorkload:
         self.setup_host()
         self.copies = max(2, math.ceil(3 * L2_BYTES / max(self.in_bytes, 1)))
         self.dev_inputs = [tuple(t.to(dev) for t in self.host) for _ in range(self.copies)]
-        self.pinned = tuple(t.pin_memory() for t in self.host)
+        self.e2e_in = tuple(t.pin_memory() for t in self.host)
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
@@ -164,6 +164,50 @@ class OpWorkload:
                 self.call(*inp)
             self.graphs.append(g)
         self.i = 0
+
+    def e2e_loop(self, dev, n: int):
+        """n end-to-end steps through the public API: each step's inputs are copied from pinned host
+        memory, the library functions run forward and backward on them, and every result is copied
+        back into pinned host memory.  The copies run on their own streams, so step i+1's
+        host->device copy and step i-1's device->host copy overlap step i's kernels (two device
+        input sets and two host result sets alternate).  Returns (h2d, d2h) bytes per step."""
+        main = torch.cuda.current_stream()
+        if not hasattr(self, "e2e_dev"):
+            self.h2d_stream, self.d2h_stream = torch.cuda.Stream(), torch.cuda.Stream()
+            self.e2e_dev = [[torch.empty_like(t, device=dev) for t in self.e2e_in] for _ in range(2)]
+            self.e2e_out = [None, None]
+        loaded = [torch.cuda.Event(), torch.cuda.Event()]
+        consumed = [torch.cuda.Event(), torch.cuda.Event()]
+
+        def load(i):
+            k = i % 2
+            with torch.cuda.stream(self.h2d_stream), torch.no_grad():
+                if i >= 2:
+                    self.h2d_stream.wait_event(consumed[k])
+                for d, h in zip(self.e2e_dev[k], self.e2e_in):
+                    d.copy_(h, non_blocking=True)
+                loaded[k].record()
+
+        self.h2d_stream.wait_stream(main)     # the previous loop's kernels are done with the inputs
+        load(0)
+        d2h = 0
+        for i in range(n):
+            k = i % 2
+            if i + 1 < n:
+                load(i + 1)
+            main.wait_event(loaded[k])
+            res = self.e2e_compute(self.e2e_dev[k])
+            consumed[k].record(main)
+            if self.e2e_out[k] is None:
+                self.e2e_out[k] = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
+            with torch.cuda.stream(self.d2h_stream):
+                self.d2h_stream.wait_stream(main)
+                for h, r in zip(self.e2e_out[k], res):
+                    r.record_stream(self.d2h_stream)
+                    h.copy_(r.detach(), non_blocking=True)
+            d2h = sum(r.numel() * r.element_size() for r in res)
+        main.wait_stream(self.d2h_stream)
+        return sum(t.numel() * t.element_size() for t in self.e2e_in), d2h
 
     def step(self, timed=None):
         g = self.graphs[self.i % self.copies]
@@ -200,15 +244,14 @@ class RMSNormWorkload(OpWorkload):
         y, rstd = torch.ops.krsi.rmsnorm_fwd(x, w, 1e-6)
         return torch.ops.krsi.rmsnorm_bwd(g, x, w, rstd)
 
-    def e2e_step(self, dev):
+    def e2e_compute(self, inputs):
         import rmsnorm
 
-        x, w, g = (t.to(dev, non_blocking=True) for t in self.pinned)
+        x, w, g = inputs
         xr, wr = x.requires_grad_(True), w.requires_grad_(True)
         y = rmsnorm.rmsnorm(xr, wr, 1e-6)
         dx, dw = torch.autograd.grad(y, [xr, wr], g)
-        res = [y.detach().to("cpu"), dx.to("cpu"), dw.to("cpu")]
-        return res, sum(t.numel() * 4 for t in self.pinned), sum(t.numel() * 4 for t in res)
+        return [y.detach(), dx, dw]
 
     def cpu_sample(self):
         from oracle import ops as O
@@ -244,15 +287,14 @@ class GegluWorkload(RMSNormWorkload):
         torch.ops.krsi.geglu_fwd(u)
         return torch.ops.krsi.geglu_bwd(g, u)
 
-    def e2e_step(self, dev):
+    def e2e_compute(self, inputs):
         import geglu
 
-        u, g = (t.to(dev, non_blocking=True) for t in self.pinned)
+        u, g = inputs
         ur = u.requires_grad_(True)
         out = geglu.geglu(ur)
         (du,) = torch.autograd.grad(out, [ur], g)
-        res = [out.detach().to("cpu"), du.to("cpu")]
-        return res, sum(t.numel() * 2 for t in self.pinned), sum(t.numel() * 2 for t in res)
+        return [out.detach(), du]
 
     def cpu_sample(self):
         from oracle import ops as O
@@ -299,7 +341,7 @@ class AttnWorkload(OpWorkload):
         self.setup_host()
         self.copies = max(2, math.ceil(3 * L2_BYTES / max(self.in_bytes, 1)))
         self.dev_inputs = [tuple(t.to(dev) for t in self.host) for _ in range(self.copies)]
-        self.pinned = tuple(t.pin_memory() for t in self.host)
+        self.e2e_in = tuple(t.pin_memory() for t in (self.host[:2] if self.fwd_only else self.host))
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
@@ -372,19 +414,15 @@ class AttnWorkload(OpWorkload):
                      fwd_bwd_tflops_14bhl2d=14 * self.B * self.H * self.S ** 2 * self.D / ((f + b) / 1e3) / 1e12)
         return {"breakdown": d}
 
-    def e2e_step(self, dev):
+    def e2e_compute(self, inputs):
         import relpos_attention as ra
 
-        qkv, pd, dout = (t.to(dev, non_blocking=True) for t in self.pinned)
-        q, p = qkv.requires_grad_(True), pd.requires_grad_(True)
+        q, p = inputs[0].requires_grad_(True), inputs[1].requires_grad_(True)
         out = ra.relpos_attention(q, p, self.B, self.S, self.H, self.D, self.scale)
         if self.fwd_only:
-            res = [out.detach().to("cpu")]
-        else:
-            dq, dp = torch.autograd.grad(out, [q, p], dout)
-            res = [out.detach().to("cpu"), dq.to("cpu"), dp.to("cpu")]
-        h2d = sum(t.numel() * t.element_size() for t in (self.pinned if not self.fwd_only else self.pinned[:2]))
-        return res, h2d, sum(t.numel() * t.element_size() for t in res)
+            return [out.detach()]
+        dq, dp = torch.autograd.grad(out, [q, p], inputs[2])
+        return [out.detach(), dq, dp]
 
     def cpu_sample(self):
         """One batch element (B=1) of the config on the reference's torch path in fp32 (the math
@@ -517,13 +555,17 @@ class BlockWorkload:
         return {"breakdown": getattr(self, "_attn", {}),
                 "model_tflops": self.work / (self._step_ms / 1e3) / 1e12 if getattr(self, "_step_ms", None) else None}
 
-    def e2e_step(self, dev):
+    def e2e_loop(self, dev, n: int):
+        """n training steps through the public API, each copying its batch shard from pinned host
+        memory and reading the loss back to the host (which also ends the step).  Returns (h2d,
+        d2h) bytes per step."""
         from harness.grad_sync import train_step
 
-        x = self.x_pinned.to(dev, non_blocking=True)
-        loss = train_step(self.model, x, self.reducer, self.world, self.loss_fn)
-        val = loss.item()                 # device -> host read of the step's result
-        return [val], self.x_pinned.numel() * 2, 4
+        for _ in range(n):
+            x = self.x_pinned.to(dev, non_blocking=True)
+            loss = train_step(self.model, x, self.reducer, self.world, self.loss_fn)
+            loss.item()                   # device -> host read of the step's result
+        return self.x_pinned.numel() * 2, 4
 
     def cpu_sample(self):
         """One layer at B=1 (1024 tokens) fwd+bwd on the reference's torch path in fp32; reported
@@ -658,13 +700,11 @@ def run_krsi_arm(args, rank, world):
     torch.cuda.synchronize()
     if dist.is_initialized():
         dist.barrier()
-    wl.e2e_step(dev)
+    e2e_steps = max(1, min(args.steps, 10))
+    wl.e2e_loop(dev, 2)                   # allocates the pinned and device buffers
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    e2e_steps = max(1, min(args.steps, 10))
-    h2d = d2h = 0
-    for _ in range(e2e_steps):
-        _, h2d, d2h = wl.e2e_step(dev)
+    h2d, d2h = wl.e2e_loop(dev, e2e_steps)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / e2e_steps)
     e2e_val = (per_step_work / (e2e_ms / 1e3) / scale if wl.unit != "tok/s"

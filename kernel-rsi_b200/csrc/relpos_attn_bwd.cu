@@ -10,9 +10,11 @@
 //   bwd_prep   delta from dO and O32; zeroes the fp32 dQ accumulator.
 //   bwd_main   one CTA per (b*H + h, 128-key block); loops over the 128-query blocks with four
 //              warpgroups:
-//                warp 0      TMA producer: K and V once; Q and dO tiles per query block (2 stages)
-//                            and the block's -lse, -delta (and bias slab when not resident).  When
-//                            D leaves padding columns (D % 16 == 8) it writes K, V = 1 and Q, dO =
+//                warp 0      TMA issuer: K and V once; Q and dO tiles per query block into a
+//                            2-stage ring, as soon as the block's dK MMAs released a stage
+//                warp 3      stage finisher: publishes a stage once its loads landed, with the
+//                            block's -lse, -delta (and bias slab when not resident).  When D
+//                            leaves padding columns (D % 16 == 8) it writes K, V = 1 and Q, dO =
 //                            a three-term 16-bit split of -lse / (scale log2 e) and -delta into
 //                            padding columns D..D+2, so the S^T and dP^T MMAs produce S - lse/c
 //                            and dP - delta directly (no per-element lse/delta reads)
