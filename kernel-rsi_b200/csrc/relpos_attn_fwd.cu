@@ -16,16 +16,19 @@
 //               window is filled while the current one is read (the first item's with the softmax
 //               warps' help); sequences too long for it fall back to per-block slabs the producer
 //               writes;
-//   warp 1      TMEM owner (512 columns) and the single-thread tcgen05.mma issuer:
-//               S_t = Q_t K^T (SS, K = DP) into TMEM, O_t += P_t V (TS: P read from TMEM, one
-//               N = DP instruction per 16 keys); the next item's first S tiles are issued right
-//               after the current item's last P V, so they run while O is written out;
+//   warp 1      TMEM owner (512 columns) and the single-thread tcgen05.mma issuer.  Each S tile
+//               is computed in two halves of 64 keys: S_{t,h} = Q_t K_h^T (SS, N = 64, K = DP)
+//               and O_t += P_{t,h} V_h (TS: P read from TMEM, one N = DP instruction per 16
+//               keys).  As soon as the softmax warps hand back a half's P, its P V and the next
+//               block's Q K^T for the same half are issued, so the MMAs of one half run while
+//               the softmax warps work on the other; the next item's first S halves are issued
+//               right after the current item's last P V, so they run while O is written out;
 //   warps 4-7   softmax for query tile 0, warps 8-11 for tile 1 (one query row per thread,
-//               row = TMEM lane): S from TMEM -> bias add (paired fp32 FMAs) -> online softmax
-//               with the rescale of O skipped unless the running max grows by more than 2^8;
-//               exp2 on the SFU for 3/4 of the elements and on the FMA pipe (sm100.cuh) for
-//               1/4 -> P (bf16/f16) written back over S in TMEM -> at the item's end O / l to memory.
-// The two query tiles ping-pong so one tile's softmax overlaps the other tile's MMAs.
+//               row = TMEM lane), half by half: S from TMEM -> bias add (paired fp32 FMAs) ->
+//               online softmax with the rescale of O skipped unless the running max grows by
+//               more than 2^8; exp2 on the SFU for 3/4 of the elements and on the FMA pipe
+//               (sm100.cuh) for 1/4 -> P (bf16/f16) written back over the S half in TMEM -> at
+//               the item's end O / l to memory.
 // Every wait is bounded (watchdog.cuh); a stalled pipeline ends the CTA with an error word.
 #include <string.h>
 
@@ -44,6 +47,7 @@ using namespace sm100;
 using attn::kTileRows;
 
 constexpr int kBN = 128;            // keys per block
+constexpr int kHalf = 64;           // keys per S half: each half has its own Q K^T, softmax step and P V
 constexpr int kQTiles = 2;          // query tiles per work item
 constexpr int kItemRows = kQTiles * kTileRows;   // queries per work item
 constexpr int kThreads = 384;       // 3 warpgroups: {producer, MMA, window fill}, softmax tile 0, tile 1
@@ -63,9 +67,9 @@ struct FwdCfg {
   static constexpr uint32_t kKVOff = kQOff + kQTiles * kTile;
   static constexpr uint32_t kSlabOff = kKVOff + NS * 2 * kTile;
   static constexpr uint32_t kBarOff = kSlabOff + NS * kSlab * 4;
-  // q_full, q_empty, kv_full/empty, s_ready/p_ready/o_final/o_free per tile, drain, row_init,
-  // row_full[2], row_free[2]
-  static constexpr int kNumBars = 2 + 2 * NS + 4 * kQTiles + 1 + 1 + 2 + 2;
+  // q_full, q_empty, kv_full/empty, s_ready/p_ready/o_sync per (tile, half), o_final/o_free per
+  // tile, drain, row_init, row_full[2], row_free[2]
+  static constexpr int kNumBars = 2 + 2 * NS + 3 * 2 * kQTiles + 2 * kQTiles + 1 + 1 + 2 + 2;
   static constexpr uint32_t kMiscOff = kBarOff + kNumBars * 8;
   static constexpr uint32_t kRowOff = (kMiscOff + 16 + 15) & ~15u;  // bias windows (runtime length)
   static constexpr uint32_t kSmem = kRowOff + 1024;                 // static part + alignment slack
@@ -130,9 +134,10 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
   uint64_t* q_empty = bars + 1;
   uint64_t* kv_full = bars + 2;
   uint64_t* kv_empty = kv_full + NS;
-  uint64_t* s_ready = kv_empty + NS;
-  uint64_t* p_ready = s_ready + kQTiles;
-  uint64_t* o_final = p_ready + kQTiles;
+  uint64_t* s_ready = kv_empty + NS;            // [tile * 2 + half]: S half computed
+  uint64_t* p_ready = s_ready + 2 * kQTiles;    // [tile * 2 + half]: P half written to TMEM
+  uint64_t* o_sync = p_ready + 2 * kQTiles;     // [tile * 2 + half]: P V of that half completed
+  uint64_t* o_final = o_sync + 2 * kQTiles;
   uint64_t* o_free = o_final + kQTiles;
   uint64_t* drain = o_free + kQTiles;
   uint64_t* row_init = drain + 1;
@@ -158,9 +163,12 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
       mbar_init(&kv_full[s], RES ? 1 : 2);   // TMA expect_tx arrival (+ bias-slab arrival)
       mbar_init(&kv_empty[s], 1);            // tcgen05.commit
     }
+    for (int i = 0; i < 2 * kQTiles; ++i) {
+      mbar_init(&s_ready[i], 1);
+      mbar_init(&p_ready[i], 128);
+      mbar_init(&o_sync[i], 1);
+    }
     for (int t = 0; t < kQTiles; ++t) {
-      mbar_init(&s_ready[t], 1);
-      mbar_init(&p_ready[t], 128);
       mbar_init(&o_final[t], 1);
       mbar_init(&o_free[t], 128);
     }
@@ -262,10 +270,16 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // The whole warp runs this branch with warp-uniform descriptors and one elected lane issues each
+    // MMA and commit: measured on B200, a single-lane issue loop takes 47 cycles per M128 N64/N80 TS
+    // MMA where the tensor pipe needs 32/40.  Waits are warp-uniform so every lane takes one path.
+    {
+      auto wait = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, abort_flag, a.spin_limit));
+      };
       constexpr uint32_t fmt = F16 ? 0u : 1u;
-      constexpr uint32_t id_qk = idesc_f16(128, kBN, fmt, false, false);   // S = Q K^T: both K-major
-      constexpr uint32_t id_pv = idesc_f16(128, DP, fmt, false, true);     // O += P V: V MN-major, N = DP
+      constexpr uint32_t id_qk = idesc_f16(128, kHalf, fmt, false, false);   // S half = Q K_h^T: both K-major
+      constexpr uint32_t id_pv = idesc_f16(128, DP, fmt, false, true);       // O += P_h V_h: V MN-major, N = DP
       // Descriptors are precomputed; an issue is a constant add and the MMA itself, which keeps
       // one thread issuing at the tensor pipe's rate.
       const uint64_t q_desc = attn::kmajor_base(smem_u32(smem + C::kQOff));
@@ -273,33 +287,40 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
       const uint64_t v_desc0 = attn::mnmajor_base(smem_u32(smem + C::kKVOff + C::kTile));
       constexpr uint64_t kStageStep = (2 * C::kTile) >> 4;
       constexpr uint64_t kQTileStep = C::kTile >> 4;
-      auto issue_qk = [&](int t, int g) {
+      constexpr uint64_t kHalfRowStep = (kHalf * 32) >> 4;   // K rows 64.. of every 16-column block
+      // S_{t,h} = Q_t K^T over keys [64h, 64h + 64) of block g, into columns t*128 + 64h
+      auto issue_qk = [&](int t, int h, int g) {
         const uint64_t qd = q_desc + (uint64_t)t * kQTileStep;
-        const uint64_t kd = k_desc0 + (uint64_t)(g % NS) * kStageStep;
-        const uint32_t d = tmem + C::kSCol + t * kBN;
+        const uint64_t kd = k_desc0 + (uint64_t)(g % NS) * kStageStep + (uint64_t)h * kHalfRowStep;
+        const uint32_t d = tmem + C::kSCol + t * kBN + h * kHalf;
 #pragma unroll
         for (int kk = 0; kk < DP / 16; ++kk)
-          mma_ss(d, qd + kk * attn::kKSliceStep, kd + kk * attn::kKSliceStep, id_qk, kk > 0 ? 1u : 0u);
+          mma_ss_e(d, qd + kk * attn::kKSliceStep, kd + kk * attn::kKSliceStep, id_qk, kk > 0 ? 1u : 0u);
       };
-      auto issue_pv = [&](int t, int g, bool first) {
+      // O_t += P_{t,h} V_h: P (2 x 16-bit per column) in the first 32 columns of its S half
+      auto issue_pv = [&](int t, int h, int g, bool first) {
         const uint64_t vd = v_desc0 + (uint64_t)(g % NS) * kStageStep;
-        const uint32_t p_tmem = tmem + C::kSCol + t * kBN;   // P: 2 x 16-bit per column
+        const uint32_t p_tmem = tmem + C::kSCol + t * kBN + h * kHalf;
         const uint32_t d = tmem + C::kOCol + t * DP;
         const uint32_t acc0 = first ? 0u : 1u;
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk)
-          mma_ts(d, p_tmem + kk * 8, vd + kk * attn::kKRowStep, id_pv, kk > 0 ? 1u : acc0);
+        for (int kk = 0; kk < kHalf / 16; ++kk)
+          mma_ts_e(d, p_tmem + kk * 8, vd + (h * (kHalf / 16) + kk) * attn::kKRowStep, id_pv, kk > 0 ? 1u : acc0);
       };
-      bool ok = my_items > 0 && mbar_wait_bounded(q_full, 0, abort_flag, a.spin_limit) &&
-                mbar_wait_bounded(&kv_full[0], 0, abort_flag, a.spin_limit);
+      bool ok = my_items > 0 && wait(q_full, 0) &&
+                wait(&kv_full[0], 0);
       if (ok) {
         tc_fence_after();
-        for (int t = 0; t < kQTiles; ++t) {
-          issue_qk(t, 0);
-          mma_commit(&s_ready[t]);
-        }
-        if (n_kb == 1) mma_commit(q_empty);   // item 0's only Q K^T is issued
+        for (int h = 0; h < 2; ++h)
+          for (int t = 0; t < kQTiles; ++t) {
+            issue_qk(t, h, 0);
+            mma_commit_e(&s_ready[2 * t + h]);
+          }
+        if (n_kb == 1) mma_commit_e(q_empty);   // item 0's only Q K^T is issued
       }
+      // Per block, the halves are served in the order (t0, h0), (t1, h0), (t0, h1), (t1, h1): P V of
+      // a half, then (inside an item) the next block's Q K^T into the same S half, so the softmax
+      // warps work on one half while the other half's MMAs run.
       int g = 0;
       for (int k = 0; k < my_items && ok; ++k) {
         for (int j = 0; j < n_kb && ok; ++j, ++g) {
@@ -307,57 +328,50 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
           const bool last_j = j + 1 == n_kb;
           const bool has_next = !last_j || k + 1 < my_items;
           auto wait_next = [&]() {   // K/V of block g + 1 (and, for a new item, its Q) landed
-            return mbar_wait_bounded(&kv_full[(g + 1) % NS], ((g + 1) / NS) & 1, abort_flag, a.spin_limit) &&
-                   (!last_j || mbar_wait_bounded(q_full, (k + 1) & 1, abort_flag, a.spin_limit));
+            return wait(&kv_full[(g + 1) % NS], ((g + 1) / NS) & 1) &&
+                   (!last_j || wait(q_full, (k + 1) & 1));
           };
-          if (!last_j) {
-            // inside an item: P V then the next S, tile by tile
+          for (int h = 0; h < 2 && ok; ++h)
             for (int t = 0; t < kQTiles; ++t) {
-              if (!mbar_wait_bounded(&p_ready[t], g & 1, abort_flag, a.spin_limit) ||
-                  (j == 0 && k > 0 && !mbar_wait_bounded(&o_free[t], (k - 1) & 1, abort_flag, a.spin_limit)) ||
-                  (t == 0 && !wait_next())) {
+              if (!wait(&p_ready[2 * t + h], g & 1) ||
+                  (j == 0 && h == 0 && k > 0 && !wait(&o_free[t], (k - 1) & 1)) ||
+                  (!last_j && t == 0 && h == 0 && !wait_next())) {
                 ok = false;
                 break;
               }
               tc_fence_after();
-              issue_pv(t, g, j == 0);
-              issue_qk(t, g + 1);
-              mma_commit(&s_ready[t]);
-            }
-          } else {
-            // an item's last block: both P V first (its output is written out while the next
-            // item's Q and first K/V arrive), then the next item's first S tiles
-            for (int t = 0; t < kQTiles; ++t) {
-              if (!mbar_wait_bounded(&p_ready[t], g & 1, abort_flag, a.spin_limit) ||
-                  (j == 0 && k > 0 && !mbar_wait_bounded(&o_free[t], (k - 1) & 1, abort_flag, a.spin_limit))) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              issue_pv(t, g, j == 0);
-              mma_commit(&o_final[t]);
-            }
-            if (ok && has_next) {
-              if (!wait_next()) {
-                ok = false;
+              issue_pv(t, h, g, j == 0 && h == 0);
+              mma_commit_e(&o_sync[2 * t + h]);
+              if (last_j) {
+                if (h == 1) mma_commit_e(&o_final[t]);
               } else {
-                tc_fence_after();
-                for (int t = 0; t < kQTiles; ++t) {
-                  issue_qk(t, g + 1);
-                  mma_commit(&s_ready[t]);
-                }
+                issue_qk(t, h, g + 1);
+                mma_commit_e(&s_ready[2 * t + h]);
               }
+            }
+          // an item's last block: every P V first (its output is written out while the next item's
+          // Q and first K/V arrive), then the next item's first S halves
+          if (ok && last_j && has_next) {
+            if (!wait_next()) {
+              ok = false;
+            } else {
+              tc_fence_after();
+              for (int h = 0; h < 2; ++h)
+                for (int t = 0; t < kQTiles; ++t) {
+                  issue_qk(t, h, g + 1);
+                  mma_commit_e(&s_ready[2 * t + h]);
+                }
             }
           }
           if (!ok) break;
           // the Q K^T just issued was the last one of its item: its Q may be replaced
-          if (has_next && (last_j ? n_kb == 1 : j + 2 == n_kb)) mma_commit(q_empty);
-          mma_commit(&kv_empty[g % NS]);
+          if (has_next && (last_j ? n_kb == 1 : j + 2 == n_kb)) mma_commit_e(q_empty);
+          mma_commit_e(&kv_empty[g % NS]);
         }
       }
       if (!ok && my_items > 0) watchdog_fire(kWdFwdMma);
       // Drain: every MMA issued above has completed before TMEM is released.
-      mma_commit(drain);
+      mma_commit_e(drain);
       for (uint32_t i = 0; i < a.spin_limit && !mbar_try_wait(drain, 0); ++i) {
       }
     }
@@ -398,99 +412,110 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
         bias_q = (bidx0 & 1) ? c0 + wf + bidx0 - 1 : c0 + bidx0;   // 8-byte aligned pairs
       }
       float m_run = -INFINITY, l_run = 0.f;
-      for (int j = 0; j < n_kb; ++j, ++g) {
+      for (int j = 0; j < n_kb && ok; ++j, ++g) {
         const int s = g % NS;
-        const bool w_ok = mbar_wait_bounded(&s_ready[t], g & 1, abort_flag, a.spin_limit) &&
-                          (RES || mbar_wait_bounded(&kv_full[s], (g / NS) & 1, abort_flag, a.spin_limit));
-        if (!__all_sync(0xffffffffu, w_ok)) {   // warp-uniform: TMEM loads/stores are warp-collective
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        uint32_t u[kBN];
+        for (int h = 0; h < 2; ++h) {
+          const bool w_ok = mbar_wait_bounded(&s_ready[2 * t + h], g & 1, abort_flag, a.spin_limit) &&
+                            (RES || h > 0 || mbar_wait_bounded(&kv_full[s], (g / NS) & 1, abort_flag, a.spin_limit));
+          if (!__all_sync(0xffffffffu, w_ok)) {   // warp-uniform: TMEM loads/stores are warp-collective
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sh_tmem = s_tmem + h * kHalf;
+          uint32_t u[kHalf];
+          tmem_ld32(sh_tmem, u);
+          tmem_ld32(sh_tmem + 32, u + 32);
+          tmem_wait_ld();
+          // v = s * scale * log2(e) + bias * log2(e), two columns per instruction
+          uint64_t v2[kHalf / 2];
+          if constexpr (RES) {
+            const uint64_t* bp = reinterpret_cast<const uint64_t*>(bias_q + j * kBN + h * kHalf);
 #pragma unroll
-        for (int c = 0; c < kBN; c += 32) tmem_ld32(s_tmem + c, u + c);
-        tmem_wait_ld();
-        // v = s * scale * log2(e) + bias * log2(e), two columns per instruction
-        uint64_t v2[kBN / 2];
-        if constexpr (RES) {
-          const uint64_t* bp = reinterpret_cast<const uint64_t*>(bias_q + j * kBN);
+            for (int i = 0; i < kHalf / 2; ++i)
+              v2[i] = f2_fma(f2_pack(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1])), scale2, bp[i]);
+          } else {
+            const float* slab = slabs + s * kSlab + slab_base + h * kHalf;
 #pragma unroll
-          for (int i = 0; i < kBN / 2; ++i)
-            v2[i] = f2_fma(f2_pack(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1])), scale2, bp[i]);
-        } else {
-          const float* slab = slabs + s * kSlab + slab_base;
+            for (int i = 0; i < kHalf / 2; ++i)
+              v2[i] = f2_fma(f2_pack(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1])), scale2,
+                             f2_pack(slab[2 * i], slab[2 * i + 1]));
+          }
+          const int valid = a.S - j * kBN - h * kHalf;      // keys of this half inside the sequence
+          if (valid < kHalf) {                              // only the last block of a ragged sequence
 #pragma unroll
-          for (int i = 0; i < kBN / 2; ++i)
-            v2[i] = f2_fma(f2_pack(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1])), scale2,
-                           f2_pack(slab[2 * i], slab[2 * i + 1]));
-        }
-        const int valid = a.S - j * kBN;                  // keys of this block inside the sequence
-        if (valid < kBN) {                                // only the last block of a ragged sequence
+            for (int i = 0; i < kHalf / 2; ++i) {
+              float lo, hi;
+              f2_unpack(v2[i], lo, hi);
+              v2[i] = f2_pack(2 * i < valid ? lo : -INFINITY, 2 * i + 1 < valid ? hi : -INFINITY);
+            }
+          }
+          // row max: 3-input max, 4 independent chains
+          float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-          for (int i = 0; i < kBN / 2; ++i) {
+          for (int i = 0; i < kHalf / 2; ++i) {
             float lo, hi;
             f2_unpack(v2[i], lo, hi);
-            v2[i] = f2_pack(2 * i < valid ? lo : -INFINITY, 2 * i + 1 < valid ? hi : -INFINITY);
+            mxa[i % 4] = max3(mxa[i % 4], lo, hi);
           }
-        }
-        // row max: 3-input max, 4 independent chains
-        float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-        for (int i = 0; i < kBN / 2; ++i) {
-          float lo, hi;
-          f2_unpack(v2[i], lo, hi);
-          mxa[i % 4] = max3(mxa[i % 4], lo, hi);
-        }
-        const float mx = fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3]));
-        const float m_new = fmaxf(m_run, mx);
-        const bool need = m_new - m_run > kRescaleThreshold;   // true on the first block (m_run = -inf)
-        float alpha = 1.f, m_use = m_run;
-        const bool warp_rescale = __any_sync(0xffffffffu, need);
-        if (warp_rescale) {
-          m_use = m_new;
-          alpha = ex2_approx(m_run - m_new);              // 0 on the first block
-        }
-        // p = 2^(v - m): three of every four pairs on the SFU, one on the FMA pipe (balances the
-        // SFU against the issue slots); row sum in 4 paired chains; P packed to 16-bit pairs
-        const uint64_t negm2 = f2_pack(-m_use, -m_use);
-        uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
-        uint32_t pk[kBN / 2];
-#pragma unroll
-        for (int i = 0; i < kBN / 2; ++i) {
-          float x0, x1, p0, p1;
-          f2_unpack(f2_add(v2[i], negm2), x0, x1);
-          if (i % 4 == 3) {
-            exp2_poly3_x2(x0, x1, p0, p1);
-          } else {
-            p0 = ex2_approx(x0);
-            p1 = ex2_approx(x1);
+          const float mx = fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3]));
+          const float m_new = fmaxf(m_run, mx);
+          // true on the item's first half (m_run = -inf); a fully masked half (m_new = m_run) never
+          const bool need = m_new - m_run > kRescaleThreshold;
+          float alpha = 1.f, m_use = m_run;
+          const bool warp_rescale = __any_sync(0xffffffffu, need);
+          if (warp_rescale) {
+            m_use = m_new;
+            alpha = ex2_approx(m_run - m_new);              // 0 on the first half
           }
-          acc2[i % 4] = f2_add(acc2[i % 4], f2_pack(p0, p1));
-          pk[i] = F16 ? pack_f16x2(p0, p1) : pack_bf16x2(p0, p1);
-        }
-        float sum_lo, sum_hi;
-        f2_unpack(f2_add(f2_add(acc2[0], acc2[1]), f2_add(acc2[2], acc2[3])), sum_lo, sum_hi);
-        const float sum = sum_lo + sum_hi;
-        l_run = l_run * alpha + sum;
-        m_run = m_use;
-        tmem_st32(s_tmem, pk);
-        tmem_st32(s_tmem + 32, pk + 32);
-        if (warp_rescale && j > 0) {
-          // O_t holds the sum through block j-1 (PV(t, j-1) completed before S_t(j) was ready).
+          // p = 2^(v - m): three of every four pairs on the SFU, one on the FMA pipe (balances the
+          // SFU against the issue slots); row sum in 4 paired chains; P packed to 16-bit pairs
+          const uint64_t negm2 = f2_pack(-m_use, -m_use);
+          uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
+          uint32_t pk[kHalf / 2];
 #pragma unroll
-          for (int c = 0; c < DP; c += 16) {
-            uint32_t ov[16];
-            tmem_ld16(o_tmem + c, ov);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 16; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-            tmem_st16(o_tmem + c, ov);
+          for (int i = 0; i < kHalf / 2; ++i) {
+            float x0, x1, p0, p1;
+            f2_unpack(f2_add(v2[i], negm2), x0, x1);
+            if (i % 4 == 3) {
+              exp2_poly3_x2(x0, x1, p0, p1);
+            } else {
+              p0 = ex2_approx(x0);
+              p1 = ex2_approx(x1);
+            }
+            acc2[i % 4] = f2_add(acc2[i % 4], f2_pack(p0, p1));
+            pk[i] = F16 ? pack_f16x2(p0, p1) : pack_bf16x2(p0, p1);
           }
+          float sum_lo, sum_hi;
+          f2_unpack(f2_add(f2_add(acc2[0], acc2[1]), f2_add(acc2[2], acc2[3])), sum_lo, sum_hi);
+          const float sum = sum_lo + sum_hi;
+          l_run = l_run * alpha + sum;
+          m_run = m_use;
+          tmem_st32(sh_tmem, pk);
+          if (warp_rescale && (j > 0 || h > 0)) {
+            // O_t must hold exactly the P V of every earlier half.  The previous half's P V is
+            // the last one issued for this tile: wait for it (the one before it completed before
+            // this half's S was computed), then scale O_t.
+            const int hp = h ^ 1, gp = h ? g : g - 1;
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(&o_sync[2 * t + hp], gp & 1, abort_flag, a.spin_limit))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < DP; c += 16) {
+              uint32_t ov[16];
+              tmem_ld16(o_tmem + c, ov);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 16; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+              tmem_st16(o_tmem + c, ov);
+            }
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(&p_ready[2 * t + h]);
         }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(&p_ready[t]);
       }
       if (!ok) break;
       if constexpr (RES) mbar_arrive(&row_free[k & 1]);   // this item's window is no longer read
