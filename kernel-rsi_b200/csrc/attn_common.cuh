@@ -161,6 +161,24 @@ inline bool make_head_map(CUtensorMap* map, const void* base, int64_t row_stride
   return r == CUDA_SUCCESS;
 }
 
+// 4-D view (D, n_heads, S, B) of a token-major 16-bit tensor like make_head_map, with box
+// (D, 1, 128, 1) and no swizzle: a dense [128 rows x D] tile, for TMA stores of whole head rows.
+// Rows >= S are outside the tensor and are not written.
+inline bool make_head_rows_map(CUtensorMap* map, const void* base, int64_t row_stride, int64_t B, int64_t S,
+                               int64_t n_heads, int64_t D, bool f16) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc || D > 256) return false;
+  memset(map, 0, sizeof(*map));
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)n_heads, (cuuint64_t)S, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)row_stride * 2, (cuuint64_t)(S * row_stride * 2)};
+  cuuint32_t box[4] = {(cuuint32_t)D, 1, (cuuint32_t)kTileRows, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // 3-D fp32 view (D, S, B) of head `h` columns of a [B*S, n_heads*D] fp32 tensor, for the TMA
 // reduce-add of a [128 rows x D] tile: element (d, s, b) at base + ((b*S + s)*n_heads*D + d), the
 // caller adds h*D to the x coordinate.  Box = (D, 128, 1), no swizzle (row-major tile with a D*4-byte

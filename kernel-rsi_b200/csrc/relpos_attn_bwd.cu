@@ -85,7 +85,7 @@ struct BwdCfg {
   static constexpr int kSlab0 = 256, kSlab1 = 256 + 256 + kCopyBank;
   static constexpr uint32_t kVecBytes = (kSlab1 + 256) * 4;
   static constexpr uint32_t kBarOff = kVecOff + NQS * kVecBytes;
-  static constexpr int kNumBars = 1 + 3 * NQS + 11;
+  static constexpr int kNumBars = 1 + 3 * NQS + 13;
   static constexpr uint32_t kMiscOff = kBarOff + kNumBars * 8;
   static constexpr uint32_t kRowOff = (kMiscOff + 16 + 15) & ~15u;   // resident rows (runtime length)
   static constexpr uint32_t kSmem = kRowOff + 1024;                  // + the 1 KB alignment slack
@@ -146,7 +146,8 @@ __device__ __forceinline__ uint4 split3(float v) {
 template <int DP, bool F16, bool RES, bool FOLD>
 __global__ void __launch_bounds__(kThreads, 1)
 relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap omap,
-                       const __grid_constant__ CUtensorMap dqmap, const BwdArgs a) {
+                       const __grid_constant__ CUtensorMap dqmap, const __grid_constant__ CUtensorMap kvmap,
+                       const BwdArgs a) {
   using C = BwdCfg<DP>;
   constexpr int NQS = C::NQS;
   extern __shared__ uint8_t smem_raw[];
@@ -167,6 +168,7 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
   uint64_t* row_full = s_ready + 8;
   uint64_t* stg_free = s_ready + 9;          // dQ staging tile read by the previous reduce-add (leader)
   uint64_t* stg_full = s_ready + 10;         // dQ staging tile written (128 dQ threads)
+  uint64_t* kv_stg = s_ready + 11;           // [2] dK / dV rows staged for their TMA store (128 each)
   float* rev0 = reinterpret_cast<float*>(smem + C::kRowOff);
   float* rev1 = rev0 + rev_row_floats(a.S);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
@@ -195,6 +197,8 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
     mbar_init(row_full, kRowFillers);
     mbar_init(stg_free, 1);
     mbar_init(stg_full, 128);
+    mbar_init(&kv_stg[0], 128);
+    mbar_init(&kv_stg[1], 128);
     abort_flag[0] = 0;
     abort_flag[1] = 0;
     fence_barrier_init();
@@ -203,6 +207,7 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
     prefetch_tensormap(&qmap);
     prefetch_tensormap(&omap);
     prefetch_tensormap(&dqmap);
+    prefetch_tensormap(&kvmap);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -226,13 +231,14 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
     mbar_arrive(row_full);
   };
 
-  // dK (scaled) or dV of key row kr, TMEM -> dqkv; run by one compute warpgroup each at the end.
+  // dK (scaled) or dV of key row kr, TMEM -> dqkv; run by one compute warpgroup each at the end.  The
+  // rows are staged as a dense [128 x D] tile in the Q/dO stage memory (free once every MMA has
+  // completed) and written by one TMA store per warpgroup: whole 144-byte head rows instead of a
+  // 16-byte store per thread and row.  Rows past the sequence end are clipped by the TMA.
   auto store_dkdv = [&](const int which, const int kr, const uint32_t lane_addr) {
     using T = typename std::conditional<F16, __half, __nv_bfloat16>::type;
-    const int key = k0 + kr;
-    const bool row_ok = key < a.S;
-    T* dst = reinterpret_cast<T*>(a.dqkv) + ((size_t)b * a.S + (row_ok ? key : 0)) * a.dqkv_stride +
-             (size_t)(1 + which) * a.H * a.D + (size_t)h * a.D;
+    T* tile = reinterpret_cast<T*>(smem + C::kQOff + which * (C::kTile * NQS));   // [128][D]
+    T* row = tile + (size_t)kr * a.D;
     const uint32_t src = tmem + lane_addr + (which == 0 ? C::kDK : C::kDV);
     const float mul = which == 0 ? a.scale : 1.f;
 #pragma unroll
@@ -242,7 +248,7 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
       tmem_wait_ld();
 #pragma unroll
       for (int e = 0; e < 16; e += 8) {
-        if (row_ok && c + e < a.D) {
+        if (c + e < a.D) {
           float f[8];
 #pragma unroll
           for (int k = 0; k < 8; ++k) f[k] = __uint_as_float(u[e + k]) * mul;
@@ -251,8 +257,19 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
                                pack_f16x2(f[6], f[7]))
                   : make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
                                pack_bf16x2(f[6], f[7]));
-          *reinterpret_cast<uint4*>(dst + c + e) = pk;
+          *reinterpret_cast<uint4*>(row + c + e) = pk;
         }
+      }
+    }
+    fence_async_shared();   // staged rows -> visible to the TMA unit
+    mbar_arrive(&kv_stg[which]);
+    if (kr == 0) {   // one thread per warpgroup issues the store once all 128 rows are staged
+      if (mbar_wait_bounded(&kv_stg[which], 0, abort_flag, a.spin_limit)) {
+        tma_store_4d(&kvmap, tile, 0, (1 + which) * a.H + h, k0, b);
+        bulk_commit_group();
+        bulk_wait_read_all();   // the tile must stay in place until the TMA has read it
+      } else {
+        watchdog_fire(kWdBwdCompute);
       }
     }
   };
@@ -503,8 +520,8 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
       const bool full = keys_full && q0 + kBlk <= a.S;
       const int qvalid = a.S - q0 - qh;        // queries of this warpgroup inside the sequence
 
-      // P^T = exp2(s2 - lse) in paired fp32, 32 queries at a time (bounded register use); three
-      // of every four pairs on the SFU, one on the FMA pipe; 16-bit copy over S^T in TMEM
+      // P^T = exp2(s2 - lse) in paired fp32, 32 queries at a time (bounded register use), exp2 on
+      // the SFU (measured faster here than moving a share to the FMA pipe); 16-bit copy over S^T
       uint64_t p2[kHalf / 2];
 #pragma unroll
       for (int qc = 0; qc < kHalf / 32; ++qc) {
@@ -523,12 +540,8 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
             if constexpr (!FOLD) x = f2_add(x, tq ? nl.y : nl.x);
             float x0, x1, y0, y1;
             f2_unpack(x, x0, x1);
-            if (e % 4 == 3) {
-              exp2_poly3_x2(x0, x1, y0, y1);
-            } else {
-              y0 = ex2_approx(x0);
-              y1 = ex2_approx(x1);
-            }
+            y0 = ex2_approx(x0);
+            y1 = ex2_approx(x1);
             if (!full) {
               y0 = (key_ok && 2 * pe < qvalid) ? y0 : 0.f;
               y1 = (key_ok && 2 * pe + 1 < qvalid) ? y1 : 0.f;
@@ -801,8 +814,8 @@ inline WsLayout ws_layout(int64_t B, int64_t S, int64_t H, int64_t D) {
 }
 
 template <int DP, bool F16>
-int launch_bwd(const CUtensorMap& qm, const CUtensorMap& om, const CUtensorMap& dqm, const BwdArgs& a, const void* dout,
-               const float* out32, float* dpd, cudaStream_t stream) {
+int launch_bwd(const CUtensorMap& qm, const CUtensorMap& om, const CUtensorMap& dqm, const CUtensorMap& kvm,
+               const BwdArgs& a, const void* dout, const float* out32, float* dpd, cudaStream_t stream) {
   using C = BwdCfg<DP>;
   const int64_t tokens_heads = (int64_t)a.B * a.S * a.H;
   relpos_bwd_prep_kernel<F16><<<(unsigned)((tokens_heads + 31) / 32), 32 * (a.D / 8), 0, stream>>>(
@@ -815,7 +828,7 @@ int launch_bwd(const CUtensorMap& qm, const CUtensorMap& om, const CUtensorMap& 
                   : (fold ? relpos_bwd_main_kernel<DP, F16, false, true> : relpos_bwd_main_kernel<DP, F16, false, false>);
   const size_t smem = res ? res_smem : C::kSmem;
   KRSI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  kern<<<dim3(a.n_blk, a.B * a.H), kThreads, smem, stream>>>(qm, om, dqm, a);
+  kern<<<dim3(a.n_blk, a.B * a.H), kThreads, smem, stream>>>(qm, om, dqm, kvm, a);
   KRSI_LAUNCH_CHECK();
   const int64_t rows = (int64_t)a.B * a.S;
   const int64_t items = rows * (a.H * a.D / 8);
@@ -831,12 +844,12 @@ int launch_bwd(const CUtensorMap& qm, const CUtensorMap& om, const CUtensorMap& 
 }
 
 template <bool F16>
-int dispatch_dp(int DP, const CUtensorMap& qm, const CUtensorMap& om, const CUtensorMap& dqm, const BwdArgs& a,
-                const void* dout, const float* out32, float* dpd, cudaStream_t s) {
+int dispatch_dp(int DP, const CUtensorMap& qm, const CUtensorMap& om, const CUtensorMap& dqm, const CUtensorMap& kvm,
+                const BwdArgs& a, const void* dout, const float* out32, float* dpd, cudaStream_t s) {
   switch (DP) {
-    case 32: return launch_bwd<32, F16>(qm, om, dqm, a, dout, out32, dpd, s);
-    case 64: return launch_bwd<64, F16>(qm, om, dqm, a, dout, out32, dpd, s);
-    case 80: return launch_bwd<80, F16>(qm, om, dqm, a, dout, out32, dpd, s);
+    case 32: return launch_bwd<32, F16>(qm, om, dqm, kvm, a, dout, out32, dpd, s);
+    case 64: return launch_bwd<64, F16>(qm, om, dqm, kvm, a, dout, out32, dpd, s);
+    case 80: return launch_bwd<80, F16>(qm, om, dqm, kvm, a, dout, out32, dpd, s);
     default: return KRSI_ERR_UNSUPPORTED;
   }
 }
@@ -875,11 +888,12 @@ extern "C" int krsi_relpos_attn_bwd(const void* dout, const void* qkv, int64_t q
   const WsLayout ws = ws_layout(B, S, H, D);
   if (!workspace || workspace_bytes < ws.total || !aligned16(workspace)) return KRSI_ERR_WORKSPACE;
   uint8_t* w = static_cast<uint8_t*>(workspace);
-  CUtensorMap qm, om, dqm;
+  CUtensorMap qm, om, dqm, kvm;
   const bool f16 = dtype == KRSI_F16;
   if (!attn::make_head_map(&qm, qkv, qkv_row_stride, B, S, 3 * H, D, f16) ||
       !attn::make_head_map(&om, dout, H * D, B, S, H, D, f16) ||
-      !attn::make_rows_f32_map(&dqm, reinterpret_cast<float*>(w + ws.dq), B, S, H, D))
+      !attn::make_rows_f32_map(&dqm, reinterpret_cast<float*>(w + ws.dq), B, S, H, D) ||
+      !attn::make_head_rows_map(&kvm, dqkv, dqkv_row_stride, B, S, 3 * H, D, f16))
     return KRSI_ERR_CUDA;
   BwdArgs a{pd,
             lse,
@@ -897,6 +911,6 @@ extern "C" int krsi_relpos_attn_bwd(const void* dout, const void* qkv, int64_t q
             scale * 1.4426950408889634f,
             scale,
             kSpinLimit};
-  return f16 ? dispatch_dp<true>(DP, qm, om, dqm, a, dout, out32, dpd, stream)
-             : dispatch_dp<false>(DP, qm, om, dqm, a, dout, out32, dpd, stream);
+  return f16 ? dispatch_dp<true>(DP, qm, om, dqm, kvm, a, dout, out32, dpd, stream)
+             : dispatch_dp<false>(DP, qm, om, dqm, kvm, a, dout, out32, dpd, stream);
 }
