@@ -100,7 +100,7 @@ struct BwdArgs {
   const float* delta;
   float* dq_acc;          // [B*S, H*D] fp32 (the main kernel adds into it through its tensor map)
   float* dbias_part;      // [B*H, n_kb, n_qb, kWarpsPerTile, kBins]
-  float* dpd_rows;        // [H, 2 n_blk - 1, 256]: per tile-diagonal sums (dBias reduction stage 1)
+  float* dpd_rows;        // [H, 2 n_blk - 1, batch chunks, 256]: per tile-diagonal sums (dBias stage 1)
   void* dqkv;
   int64_t dqkv_stride;
   int B, S, H, D, n_blk;
@@ -749,19 +749,24 @@ relpos_bwd_dq_kernel(const float* __restrict__ dq_acc, void* __restrict__ dqkv, 
   *reinterpret_cast<uint4*>(reinterpret_cast<T*>(dqkv) + row * dqkv_stride + c) = pk;
 }
 
-// dBias reduction, stage 1: one CTA per (tile diagonal d = kb - qb, head h).  Thread (w, j) sums
-// bin j of warp w over the batch and the tiles on diagonal d (each tile's 8 x 96 bins are one
-// contiguous 3 KB row, so the CTA's loads are coalesced); then, per tile diagonal e = key - query in
-// [-127, 127], the bins holding e (warp (half, quarter) keeps e in bin 32 quarter - 64 half + 31 - e)
-// are added in warp order.  rows[h, d + nb - 1, e + 127].  Fixed order: deterministic.
+// dBias reduction, stage 1: one CTA per (tile diagonal d = kb - qb, head h, batch chunk c).  Thread
+// (w, j) sums bin j of warp w over the chunk's batch elements and the tiles on diagonal d (each
+// tile's 8 x 96 bins are one contiguous 3 KB row, so the CTA's loads are coalesced); then, per tile
+// diagonal e = key - query in [-127, 127], the bins holding e (warp (half, quarter) keeps e in bin
+// 32 quarter - 64 half + 31 - e) are added in warp order.  rows[h, d + nb - 1, c, e + 127].  The
+// batch is split into up to kDiagChunks chunks so that enough CTAs stream the partials (one CTA per
+// (d, h) left most SMs idle); fixed order throughout: deterministic.
 constexpr int kDiagThreads = kWarpsPerTile * kBins;   // 768
+constexpr int kDiagChunks = 8;
+__host__ __device__ inline int diag_chunks(int B) { return B < kDiagChunks ? B : kDiagChunks; }
 __global__ void __launch_bounds__(kDiagThreads)
 relpos_bwd_dpd_diag_kernel(const float* __restrict__ part, float* __restrict__ rows, int B, int H, int nb) {
   __shared__ float acc[kDiagThreads];
-  const int d = (int)blockIdx.x - (nb - 1), h = blockIdx.y;
+  const int d = (int)blockIdx.x - (nb - 1), h = blockIdx.y, c = blockIdx.z, nc = diag_chunks(B);
   const int kb_lo = d > 0 ? d : 0, kb_hi = d > 0 ? nb : nb + d;   // qb = kb - d in [0, nb)
+  const int bb_lo = c * B / nc, bb_hi = (c + 1) * B / nc;
   float s = 0.f;
-  for (int bb = 0; bb < B; ++bb) {
+  for (int bb = bb_lo; bb < bb_hi; ++bb) {
     const float* pb = part + (size_t)(bb * H + h) * nb * nb * kDiagThreads;
     for (int kb = kb_lo; kb < kb_hi; ++kb) s += __ldg(pb + ((size_t)kb * nb + (kb - d)) * kDiagThreads + threadIdx.x);
   }
@@ -775,14 +780,15 @@ relpos_bwd_dpd_diag_kernel(const float* __restrict__ part, float* __restrict__ r
       const int j = 32 * (w % 4) - 64 * (w / 4) + 31 - e;
       if (j >= 0 && j < kBins) v += acc[w * kBins + j];
     }
-    rows[((size_t)h * (2 * nb - 1) + blockIdx.x) * 256 + threadIdx.x] = v;
+    rows[(((size_t)h * (2 * nb - 1) + blockIdx.x) * nc + c) * 256 + threadIdx.x] = v;
   }
 }
 
 // dBias reduction, stage 2: dpd[h, t] for g = t - (S - 1) = key - query: the two tile diagonals
-// whose range covers g (d_hi = ceil-ish (g - 127) / 128 and d_hi - 1), added in that order.
+// whose range covers g (d_hi = ceil-ish (g - 127) / 128 and d_hi - 1), in that order, each summed
+// over the batch chunks in chunk order.
 __global__ void __launch_bounds__(256)
-relpos_bwd_dpd_kernel(const float* __restrict__ rows, float* __restrict__ dpd, int S, int H, int nb) {
+relpos_bwd_dpd_kernel(const float* __restrict__ rows, float* __restrict__ dpd, int S, int H, int nb, int nc) {
   const int h = blockIdx.y;
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= 2 * S - 1) return;
@@ -792,7 +798,8 @@ relpos_bwd_dpd_kernel(const float* __restrict__ rows, float* __restrict__ dpd, i
   for (int d = d_hi; d >= d_hi - 1; --d) {
     const int e = g - 128 * d;
     if (e < -(kBlk - 1) || e > kBlk - 1 || d <= -nb || d >= nb) continue;
-    acc += rows[((size_t)h * (2 * nb - 1) + (d + nb - 1)) * 256 + (e + kBlk - 1)];
+    const float* r = rows + ((size_t)h * (2 * nb - 1) + (d + nb - 1)) * nc * 256 + (e + kBlk - 1);
+    for (int c = 0; c < nc; ++c) acc += r[(size_t)c * 256];
   }
   dpd[(size_t)h * (2 * S - 1) + t] = acc;
 }
@@ -809,7 +816,7 @@ inline WsLayout ws_layout(int64_t B, int64_t S, int64_t H, int64_t D) {
   w.dq = up((size_t)B * H * S * 4);
   w.part = w.dq + up((size_t)B * S * H * D * 4);
   w.rows = w.part + up((size_t)B * H * nb * nb * kWarpsPerTile * kBins * 4);
-  w.total = w.rows + up((size_t)H * (2 * nb - 1) * 256 * 4);
+  w.total = w.rows + up((size_t)H * (2 * nb - 1) * diag_chunks((int)B) * 256 * 4);
   return w;
 }
 
@@ -835,10 +842,11 @@ int launch_bwd(const CUtensorMap& qm, const CUtensorMap& om, const CUtensorMap& 
   relpos_bwd_dq_kernel<F16><<<(unsigned)((items + 255) / 256), 256, 0, stream>>>(a.dq_acc, a.dqkv, a.dqkv_stride,
                                                                                   rows, a.H * a.D, a.scale);
   KRSI_LAUNCH_CHECK();
-  relpos_bwd_dpd_diag_kernel<<<dim3(2 * a.n_blk - 1, a.H), kDiagThreads, 0, stream>>>(a.dbias_part, a.dpd_rows, a.B,
-                                                                                      a.H, a.n_blk);
+  relpos_bwd_dpd_diag_kernel<<<dim3(2 * a.n_blk - 1, a.H, diag_chunks(a.B)), kDiagThreads, 0, stream>>>(
+      a.dbias_part, a.dpd_rows, a.B, a.H, a.n_blk);
   KRSI_LAUNCH_CHECK();
-  relpos_bwd_dpd_kernel<<<dim3((2 * a.S - 1 + 255) / 256, a.H), 256, 0, stream>>>(a.dpd_rows, dpd, a.S, a.H, a.n_blk);
+  relpos_bwd_dpd_kernel<<<dim3((2 * a.S - 1 + 255) / 256, a.H), 256, 0, stream>>>(a.dpd_rows, dpd, a.S, a.H, a.n_blk,
+                                                                                  diag_chunks(a.B));
   KRSI_LAUNCH_CHECK();
   return KRSI_OK;
 }
