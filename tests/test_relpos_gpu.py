@@ -156,6 +156,29 @@ def test_bwd_training_config():
     attn_bwd_check(8, 2048, 16, 72, seed=4)
 
 
+def test_block_shape_batch_split_consistency():
+    """Block shape (B=32, L=1024, H=16, D=72: ~28 CTA waves), checked through a size-independent
+    property instead of the oracle: every (b, h) is computed on its own, so the first two batch
+    elements give bit-identical out32, lse, dK and dV whether they run inside the B=32 call or as a
+    B=2 call; dQ (summed over key blocks in arrival order) agrees to rounding."""
+    import _ext
+
+    B, S, H, D = 32, 1024, 16, 72
+    sc = D ** -0.5
+    qkv, pd, dout = (t.to(dev) for t in O.attn_inputs(B, S, H, D, torch.bfloat16, seed=3))
+    out, out32, lse = torch.ops.krsi.relpos_attn_fwd(qkv, pd, B, S, H, D, sc)
+    dq1, _ = torch.ops.krsi.relpos_attn_bwd(dout, qkv, pd, out32, lse, B, S, H, D, sc)
+    n = 2 * S
+    q2, d2 = qkv[:n].contiguous(), dout[:n].contiguous()
+    o2, o32_2, lse2 = torch.ops.krsi.relpos_attn_fwd(q2, pd, 2, S, H, D, sc)
+    dq2, _ = torch.ops.krsi.relpos_attn_bwd(d2, q2, pd, o32_2, lse2, 2, S, H, D, sc)
+    torch.cuda.synchronize()
+    assert _ext.device_status(clear=True) == 0
+    assert torch.equal(out32[:n], o32_2) and torch.equal(lse[:2 * H], lse2)
+    assert torch.equal(dq1[:n, H * D:], dq2[:, H * D:])
+    assert norm_max_err(dq1[:n, :H * D].float(), dq2[:, :H * D].float()) <= 1e-2
+
+
 def test_bwd_dk_dv_dpd_deterministic():
     B, S, H, D = 2, 512, 2, 72
     qkv, pd, dout = (t.to(dev) for t in O.attn_inputs(B, S, H, D, torch.bfloat16, seed=21))
