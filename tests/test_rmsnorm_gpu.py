@@ -64,6 +64,27 @@ def test_kernel_semantics_vs_oracle(rows, n, xdt, wdt):
     assert norm_max_err(dw.cpu(), dw_o) <= (1e-5 if wdt == torch.float32 else 1e-2)
 
 
+def test_block_shape_bf16_vs_oracle():
+    """The block harness's shape and dtypes: x [32768, 1152] bf16 with a bf16 weight (the plan with
+    two 256-thread blocks per SM and shared-memory dw sums).  y, rstd and dx on 512 sampled rows
+    against the oracle (rows are independent), dw over all rows against the oracle run on the GPU in
+    float64."""
+    rows, n = 32768, 1152
+    x, w, g = O.rmsnorm_inputs(rows, n, torch.float32, seed=11)
+    x, w, g = x.to(torch.bfloat16).to(dev), w.to(torch.bfloat16).to(dev), g.to(torch.bfloat16).to(dev)
+    y, rstd = torch.ops.krsi.rmsnorm_fwd(x, w, 1e-6)
+    dx, dw = torch.ops.krsi.rmsnorm_bwd(g, x, w, rstd)
+    sel = torch.cat([torch.arange(0, 256), torch.arange(rows - 256, rows)]).to(dev)
+    y_o, r_o = O.rmsnorm_fwd(x[sel], w, 1e-6)
+    dx_o, _ = O.rmsnorm_bwd(g[sel], x[sel], w, r_o)
+    assert norm_max_err(y[sel].float(), y_o.float()) <= 1e-2
+    assert norm_max_err(rstd[sel], r_o) <= 1e-6
+    assert norm_max_err(dx[sel].float(), dx_o.float()) <= 1e-2
+    _, r_all = O.rmsnorm_fwd(x, w, 1e-6)
+    _, dw_o = O.rmsnorm_bwd(g, x, w, r_all)
+    assert norm_max_err(dw.float(), dw_o.float()) <= 1e-2
+
+
 def test_reference_selftest_criterion_bf16():
     """The reference's selftest: [4096,1024] bf16, w = 1 + 0.1 N(0,1); compare() slack 2."""
     x, w, _ = O.rmsnorm_inputs(4096, 1024, torch.float32, seed=3)
