@@ -1,9 +1,9 @@
 """Run one small case of a krsi_b200 kernel (for profilers such as ncu): three warm-up calls and
 one more, on seeded inputs.
 
-  python kernel-rsi_b200/profile_case.py rmsnorm|geglu|attn_fwd|attn ROWS_OR_B [S]
+  python kernel-rsi_b200/profile_case.py rmsnorm|rmsnorm_bf16|geglu|attn_fwd|attn ROWS_OR_B [S]
 
-rmsnorm: x [ROWS, 1152] fp32 fwd+bwd; geglu: u [ROWS, 9216] bf16 fwd+bwd;
+rmsnorm / rmsnorm_bf16: x [ROWS, 1152] fp32 / bf16 fwd+bwd; geglu: u [ROWS, 9216] bf16 fwd+bwd;
 attn_fwd / attn: relpos attention B=ROWS_OR_B, S, H=16, D=72 bf16 (fwd / fwd+bwd).
 """
 import sys
@@ -27,9 +27,10 @@ def main():
     n = int(sys.argv[2])
     ops = torch.ops.krsi
     for _ in range(4):
-        if which == "rmsnorm":
-            x, g = gen((n, 1152), 0, torch.float32), gen((n, 1152), 2, torch.float32)
-            w = gen((1152,), 1, torch.float32, 0.02, 1.0)
+        if which in ("rmsnorm", "rmsnorm_bf16"):
+            dt = torch.float32 if which == "rmsnorm" else torch.bfloat16
+            x, g = gen((n, 1152), 0, dt), gen((n, 1152), 2, dt)
+            w = gen((1152,), 1, dt, 0.02, 1.0)
             y, r = ops.rmsnorm_fwd(x, w, 1e-6)
             ops.rmsnorm_bwd(g, x, w, r)
         elif which == "geglu":
