@@ -120,6 +120,25 @@ constexpr int kBwdMinBlocks = kBwdSmemAcc<TPR, VEC, NCH> ? 2 : 1;
 template <int VEC>
 __device__ __forceinline__ int acc_idx(int c, int e, int t) { return ((c * (VEC / 4) + e / 4) * 32 + t) * 4 + e % 4; }
 
+// 16-bit warp-per-row plans also stage the warp's NEXT row of g and x in shared memory with
+// cp.async while the current row is reduced and stored, so a warp always has a row in flight
+// (the loads of the plain loop wait a full DRAM round trip per row).  Each lane copies and
+// later reads only its own 16-byte packets, so cp.async.wait_group is the only
+// synchronisation.  Stage: per warp, [x | g][NCH][32 lanes] of 16 bytes.
+template <int XT, int TPR, int VEC, int NCH>
+constexpr bool kBwdStage = kBwdSmemAcc<TPR, VEC, NCH> && sizeof(typename Elem<XT>::T) == 2 && VEC == 8;
+
+// Copies 16 bytes from global to shared.  `after` is a value computed from the registers that
+// were read out of `dst`'s slot: taking it as an operand makes the copy issue only once those
+// reads have completed, so the copy cannot overwrite the slot before it has been read.
+__device__ __forceinline__ void cp_async16_after(void* dst, const void* src, float after) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("{\n\t.reg .f32 dep;\n\tmov.f32 dep, %2;\n\tcp.async.cg.shared.global [%0], [%1], 16;\n\t}"
+               :: "r"(d), "l"(src), "f"(after) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 template <int XT, int WT, int TPR, int VEC, int NCH>
 __global__ void __launch_bounds__(RowCfg<TPR>::kThreads, kBwdMinBlocks<TPR, VEC, NCH>)
 rms_bwd_kernel(const typename Elem<XT>::T* __restrict__ g, const typename Elem<XT>::T* __restrict__ x,
@@ -128,12 +147,15 @@ rms_bwd_kernel(const typename Elem<XT>::T* __restrict__ g, const typename Elem<X
   using WE = Elem<WT>;
   using DE = Elem<Promote<XT, WT>::value>;   // dtype of the g*w product
   constexpr int RPB = RowCfg<TPR>::kRowsPerBlock;
-  extern __shared__ float smem_dw[];          // [RPB][n] when RPB > 1
+  extern __shared__ __align__(16) float smem_dw[];   // [RPB][n] when RPB > 1
   __shared__ float red[32];
   const int t = threadIdx.x % TPR;
   const int sub = threadIdx.x / TPR;
 
   constexpr bool SACC = kBwdSmemAcc<TPR, VEC, NCH>;
+  constexpr bool STAGE = kBwdStage<XT, TPR, VEC, NCH>;
+  // STAGE: this warp's stage, after the RPB accumulators
+  uint4* stg = reinterpret_cast<uint4*>(smem_dw + RPB * (NCH * VEC * 32)) + sub * (2 * NCH * 32);
   float dwv[NCH][VEC];
 #pragma unroll
   for (int c = 0; c < NCH; ++c)
@@ -147,24 +169,49 @@ rms_bwd_kernel(const typename Elem<XT>::T* __restrict__ g, const typename Elem<X
       for (int e = 0; e < VEC; e += 4) acc4[acc_idx<VEC>(c, e, t) / 4] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
 
-  for (int64_t row0 = (int64_t)blockIdx.x * RPB; row0 < rows; row0 += (int64_t)gridDim.x * RPB) {
+  const int64_t stride = (int64_t)gridDim.x * RPB;
+  if constexpr (STAGE) {   // prologue: stage this warp's first row
+    const int64_t row = (int64_t)blockIdx.x * RPB + sub;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int col = (c * TPR + t) * VEC;
+      if (row < rows && col < n) {
+        cp_async16_after(&stg[c * 32 + t], x + row * n + col, 0.f);
+        cp_async16_after(&stg[(NCH + c) * 32 + t], g + row * n + col, 0.f);
+      }
+    }
+    cp_async_commit();
+  }
+
+  for (int64_t row0 = (int64_t)blockIdx.x * RPB; row0 < rows; row0 += stride) {
     const int64_t row = row0 + sub;
     const bool live = row < rows;
     const auto* xr = x + row * n;
     const auto* gr = g + row * n;
     float xv[NCH][VEC], dn[NCH][VEC];
+    if constexpr (STAGE) cp_async_wait_all();
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
       const int col = (c * TPR + t) * VEC;
       if (live && col < n) {
-        load_vec<XT, VEC>(xr + col, xv[c], true);
-        load_vec<XT, VEC>(gr + col, dn[c], true);   // dn holds g until converted below
+        if constexpr (STAGE) {
+          using E = Elem<XT>;
+          Vec16<typename E::T> vx, vg;
+          *reinterpret_cast<uint4*>(&vx) = stg[c * 32 + t];
+          *reinterpret_cast<uint4*>(&vg) = stg[(NCH + c) * 32 + t];
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) { xv[c][e] = E::load(vx.v[e]); dn[c][e] = E::load(vg.v[e]); }
+        } else {
+          load_vec<XT, VEC>(xr + col, xv[c], true);
+          load_vec<XT, VEC>(gr + col, dn[c], true);   // dn holds g until converted below
+        }
       } else {
 #pragma unroll
         for (int e = 0; e < VEC; ++e) { xv[c][e] = 0.f; dn[c][e] = 0.f; }
       }
     }
     const float r = live ? rstd[row] : 0.f;
+    const int64_t nrow = row + stride;   // this warp's next row (STAGE: staged below)
     float dot = 0.f;
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
@@ -195,7 +242,15 @@ rms_bwd_kernel(const typename Elem<XT>::T* __restrict__ g, const typename Elem<X
         dn[c][e] = DE::round(gg * wv[e]);
         dot = fmaf(dn[c][e], xv[c][e], dot);
       }
+      if constexpr (STAGE) {   // chunk c's slots have been read (dot depends on all of them)
+        const int col = (c * TPR + t) * VEC;
+        if (nrow < rows && col < n) {
+          cp_async16_after(&stg[c * 32 + t], x + nrow * n + col, dot);
+          cp_async16_after(&stg[(NCH + c) * 32 + t], g + nrow * n + col, dot);
+        }
+      }
     }
+    if constexpr (STAGE) cp_async_commit();
     dot = row_sum<TPR>(dot, red);
     const float k = r * r * r * (dot / (float)n);
     if (live) {
@@ -212,6 +267,8 @@ rms_bwd_kernel(const typename Elem<XT>::T* __restrict__ g, const typename Elem<X
       }
     }
   }
+
+  if constexpr (STAGE) cp_async_wait_all();   // nothing is left in flight (the last group is empty)
 
   // Per-block dw partial; the RPB row groups of a block are combined in a fixed order.
   float* out = dw_part + (int64_t)blockIdx.x * n;
@@ -349,7 +406,9 @@ template <int XT, int WT, int TPR, int VEC, int NCH>
 int run_bwd(const BwdArgs& a) {
   using Cfg = RowCfg<TPR>;
   const size_t per_warp = kBwdSmemAcc<TPR, VEC, NCH> ? (size_t)NCH * VEC * 32 : (size_t)a.n;
-  const size_t smem = Cfg::kRowsPerBlock > 1 ? (size_t)Cfg::kRowsPerBlock * per_warp * sizeof(float) : 0;
+  const size_t stage = kBwdStage<XT, TPR, VEC, NCH> ? (size_t)Cfg::kRowsPerBlock * 2 * NCH * 32 * 16 : 0;
+  const size_t smem =
+      Cfg::kRowsPerBlock > 1 ? (size_t)Cfg::kRowsPerBlock * per_warp * sizeof(float) + stage : 0;
   auto kern = rms_bwd_kernel<XT, WT, TPR, VEC, NCH>;
   if (smem > 48 * 1024)
     KRSI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
