@@ -49,6 +49,12 @@ def test_baseline_config_fp32_max_abs_1e5():
     (7, 4096, torch.float16, torch.float16),
     (5, 16384, torch.float32, torch.float32),        # block-per-row plan
     (64, 1152, torch.bfloat16, torch.float32),       # mixed: bf16 activations, fp32 weight
+    # 16-bit rows whose backward stages the next row in shared memory: more rows than the
+    # 296 x 8 warps (so warps loop, with a ragged last pass), a partial last packet chunk,
+    # a one-chunk row and the widest staged row
+    (5000, 1000, torch.float16, torch.float16),
+    (2371, 40, torch.bfloat16, torch.bfloat16),
+    (3000, 1280, torch.bfloat16, torch.float32),
 ])
 def test_kernel_semantics_vs_oracle(rows, n, xdt, wdt):
     x, w, g = O.rmsnorm_inputs(rows, n, torch.float32, seed=rows + n)
