@@ -54,7 +54,7 @@ int krsi_device_status(int* status_out, int clear);
 
 /* ---------------------------------------------------------------- RMSNorm
  * y = w * (x * rstd).to(w.dtype), rstd = 1/sqrt(mean(x^2) + eps), per row.
- * Replaces library/rmsnorm.py:81-86 (_fwd -> _rms_fwd, rmsnorm.py:49-58).
+ * Replaces library/rmsnorm.py:54-59 (_fwd -> _rms_fwd, rmsnorm.py:22-31).
  * x, y: [rows, n] of x_dtype; w: [n] of w_dtype; rstd: [rows] fp32. */
 int krsi_rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd,
                      int64_t rows, int64_t n, float eps,
@@ -65,7 +65,7 @@ int krsi_rmsnorm_bwd_workspace_size(int64_t rows, int64_t n, size_t* bytes);
 
 /* dx = r*dn - x*r^3*mean(dn*x) with dn = (g*w) rounded to the promoted input type;
  * dw = sum over rows of g * (x*r).to(w.dtype), reduced deterministically in two stages.
- * Replaces library/rmsnorm.py:89-95 (_bwd -> _rms_bwd, rmsnorm.py:61-78, then dwp.sum(0)).
+ * Replaces library/rmsnorm.py:62-68 (_bwd -> _rms_bwd, rmsnorm.py:34-51, then dwp.sum(0) at :68).
  * g, x, dx: [rows, n] of x_dtype; w, dw: [n] of w_dtype; rstd: [rows] fp32. */
 int krsi_rmsnorm_bwd(const void* g, const void* x, const void* w, const float* rstd,
                      void* dx, void* dw, void* workspace, size_t workspace_bytes,
@@ -75,13 +75,14 @@ int krsi_rmsnorm_bwd(const void* g, const void* x, const void* w, const float* r
  * memory, or a loop that must not stall on cudaMalloc): the dw partial sums live in a fixed
  * device array inside this library (4 MiB per GPU that loads it, kept until the process exits)
  * instead of a caller workspace.  No counterpart in the reference (its backward allocates
- * through torch, rmsnorm.py:93).
+ * through torch, rmsnorm.py:66).
  * Limit: (dw partial rows) x n <= 1,048,576 floats.  The partial-row count is
  * min(ceil(rows / 8), 296) when one warp handles a row (rows of up to 2048 fp32 or 4096
  * 16-bit elements, 16-byte aligned) and min(rows, 296) otherwise; for example rows = 2048,
  * n = 1152 uses 256 x 1152.  Larger problems return KRSI_ERR_UNSUPPORTED.
- * The first call on each device looks up the array's address (cudaGetSymbolAddress) with that
- * device current; make that first call before any stream capture.  All calls share the array:
+ * Every call looks up the array's address (cudaGetSymbolAddress) in the current context, so a
+ * device reset never leaves a stale pointer; the first call on a device also loads the module,
+ * so make it before any stream capture.  All calls share the array:
  * calls whose kernels overlap on the GPU (different streams, same device) race and corrupt dw.
  * Allocates nothing: no cudaMalloc, cudaFree or allocating library call. */
 int krsi_rmsnorm_bwd_noalloc(const void* g, const void* x, const void* w, const float* rstd,
@@ -90,13 +91,13 @@ int krsi_rmsnorm_bwd_noalloc(const void* g, const void* x, const void* w, const 
 
 /* ---------------------------------------------------------------- GEGLU
  * out = gelu_tanh(u[:, :F]).to(dtype) * u[:, F:].
- * Replaces library/geglu.py:209-215 (_fwd -> _geglu_fwd, geglu.py:181-189).
+ * Replaces library/geglu.py:55-61 (_fwd -> _geglu_fwd, geglu.py:27-35).
  * u: [rows, 2F]; out: [rows, F]; both of `dtype`. */
 int krsi_geglu_fwd(const void* u, void* out, int64_t rows, int64_t F, int dtype,
                    cudaStream_t stream);
 
 /* du = [d(gate) | d(value)] in one [rows, 2F] tensor.
- * Replaces library/geglu.py:218-222 (_bwd -> _geglu_bwd, geglu.py:192-206).
+ * Replaces library/geglu.py:64-68 (_bwd -> _geglu_bwd, geglu.py:38-52).
  * g: [rows, F]; u, du: [rows, 2F]; all of `dtype`. */
 int krsi_geglu_bwd(const void* g, const void* u, void* du, int64_t rows, int64_t F,
                    int dtype, cudaStream_t stream);

@@ -2,10 +2,10 @@
 // elementwise kernels over the merged [gate | value] GEMM output.
 //
 // Semantics follow library/geglu.py of kernel-rsi:
-//   gelu parts (geglu.py:175-178): z = sqrt(2/pi)*(a + 0.044715 a^3);
+//   gelu parts (geglu.py:20-24): z = sqrt(2/pi)*(a + 0.044715 a^3);
 //                                  t = tanh(z) = 1 - 2/(exp(2z)+1);  gel = 0.5 a (1+t)
-//   forward  (geglu.py:181-189): out = gel.to(dtype) * b          (product rounded to dtype)
-//   backward (geglu.py:192-206): db = g * gel.to(dtype)           (rounded to dtype)
+//   forward  (geglu.py:27-35): out = gel.to(dtype) * b          (product rounded to dtype)
+//   backward (geglu.py:38-52): db = g * gel.to(dtype)           (rounded to dtype)
 //                                dgel = (g*b) rounded to dtype, then fp32
 //                                da = dgel * (0.5(1+t) + 0.5 a (1-t^2) sqrt(2/pi)(1+3*0.044715 a^2))
 //   with a = u[:, :F] (gate), b = u[:, F:] (value); du = [da | db].

@@ -2,9 +2,9 @@
 // rows held in registers, fp32 statistics, and a two-stage deterministic dweight reduction.
 //
 // Semantics follow library/rmsnorm.py of kernel-rsi:
-//   forward  (rmsnorm.py:49-58): r = 1/sqrt(sum(x^2)/n + eps); y = w * (x*r).to(w.dtype),
+//   forward  (rmsnorm.py:22-31, :54-59): r = 1/sqrt(sum(x^2)/n + eps); y = w * (x*r).to(w.dtype),
 //            stored in x's dtype; r saved per row in fp32.
-//   backward (rmsnorm.py:61-78, :95): n = (x*r).to(w.dtype); dw += g*n (fp32);
+//   backward (rmsnorm.py:34-51, :62-68): n = (x*r).to(w.dtype); dw += g*n (fp32);
 //            dn = (g*w) rounded to the promoted type of g and w, then fp32;
 //            dx = r*dn - x*r^3*sum(dn*x)/n; dw = (sum of per-block partials).to(w.dtype).
 // Layout: a row is a contiguous run of n elements handled by TPR threads (one warp for
@@ -12,7 +12,6 @@
 // VEC elements at columns (c*TPR + t)*VEC, so each load/store instruction of a row group is
 // one fully coalesced 128-bit-per-thread transaction.  NCH is a compile-time constant, so
 // the row slice stays in registers.
-#include <mutex>
 
 #include "common.cuh"
 
@@ -128,13 +127,12 @@ __device__ __forceinline__ int acc_idx(int c, int e, int t) { return ((c * (VEC 
 template <int XT, int TPR, int VEC, int NCH>
 constexpr bool kBwdStage = kBwdSmemAcc<TPR, VEC, NCH> && sizeof(typename Elem<XT>::T) == 2 && VEC == 8;
 
-// Copies 16 bytes from global to shared.  `after` is a value computed from the registers that
-// were read out of `dst`'s slot: taking it as an operand makes the copy issue only once those
-// reads have completed, so the copy cannot overwrite the slot before it has been read.
-__device__ __forceinline__ void cp_async16_after(void* dst, const void* src, float after) {
+// Copies 16 bytes from global to shared.  A slot is refilled only after the loop that reads it
+// has ended and the warp has passed __syncwarp(), which orders those shared-memory reads before
+// the copy's writes.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
-  asm volatile("{\n\t.reg .f32 dep;\n\tmov.f32 dep, %2;\n\tcp.async.cg.shared.global [%0], [%1], 16;\n\t}"
-               :: "r"(d), "l"(src), "f"(after) : "memory");
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(d), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
@@ -176,8 +174,8 @@ rms_bwd_kernel(const typename Elem<XT>::T* __restrict__ g, const typename Elem<X
     for (int c = 0; c < NCH; ++c) {
       const int col = (c * TPR + t) * VEC;
       if (row < rows && col < n) {
-        cp_async16_after(&stg[c * 32 + t], x + row * n + col, 0.f);
-        cp_async16_after(&stg[(NCH + c) * 32 + t], g + row * n + col, 0.f);
+        cp_async16(&stg[c * 32 + t], x + row * n + col);
+        cp_async16(&stg[(NCH + c) * 32 + t], g + row * n + col);
       }
     }
     cp_async_commit();
@@ -210,6 +208,7 @@ rms_bwd_kernel(const typename Elem<XT>::T* __restrict__ g, const typename Elem<X
         for (int e = 0; e < VEC; ++e) { xv[c][e] = 0.f; dn[c][e] = 0.f; }
       }
     }
+    if constexpr (STAGE) __syncwarp();   // every lane's reads of the stage precede its refills
     const float r = live ? rstd[row] : 0.f;
     const int64_t nrow = row + stride;   // this warp's next row (STAGE: staged below)
     float dot = 0.f;
@@ -242,11 +241,11 @@ rms_bwd_kernel(const typename Elem<XT>::T* __restrict__ g, const typename Elem<X
         dn[c][e] = DE::round(gg * wv[e]);
         dot = fmaf(dn[c][e], xv[c][e], dot);
       }
-      if constexpr (STAGE) {   // chunk c's slots have been read (dot depends on all of them)
+      if constexpr (STAGE) {   // chunk c's slots were read before the __syncwarp() above
         const int col = (c * TPR + t) * VEC;
         if (nrow < rows && col < n) {
-          cp_async16_after(&stg[c * 32 + t], x + nrow * n + col, dot);
-          cp_async16_after(&stg[(NCH + c) * 32 + t], g + nrow * n + col, dot);
+          cp_async16(&stg[c * 32 + t], x + nrow * n + col);
+          cp_async16(&stg[(NCH + c) * 32 + t], g + nrow * n + col);
         }
       }
     }
@@ -528,22 +527,14 @@ constexpr int64_t kNoAllocScratchFloats = 1 << 20;   // 4 MiB: (dw partial rows)
 // device with cudaGetSymbolAddress.
 static __device__ __align__(256) float g_rms_noalloc_scratch[kNoAllocScratchFloats];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_scratch_mutex;
-float* g_scratch_ptr[kMaxDevices] = {};
-
-// Device address of the scratch array on the current device, looked up once per device.
+// Device address of the scratch array in the current context.  It is looked up on every call
+// (a host-side table lookup once the module is loaded) rather than cached, so a pointer never
+// outlives the context it belongs to (cudaDeviceReset, a torn-down primary context).  The first
+// call on a device loads the module and must therefore come before any stream capture.
 int noalloc_scratch(float** out) {
-  int dev = 0;
-  KRSI_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= kMaxDevices) return KRSI_ERR_UNSUPPORTED;
-  std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (!g_scratch_ptr[dev]) {
-    void* p = nullptr;
-    KRSI_CUDA_TRY(cudaGetSymbolAddress(&p, g_rms_noalloc_scratch));
-    g_scratch_ptr[dev] = static_cast<float*>(p);
-  }
-  *out = g_scratch_ptr[dev];
+  void* p = nullptr;
+  KRSI_CUDA_TRY(cudaGetSymbolAddress(&p, g_rms_noalloc_scratch));
+  *out = static_cast<float*>(p);
   return KRSI_OK;
 }
 

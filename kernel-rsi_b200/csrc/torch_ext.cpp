@@ -1,7 +1,7 @@
 // torch_ext.cpp - thin torch binding of the krsi_b200 C ABI.
 //
 // Registers the operator names and schemas the reference registers through
-// torch.library.triton_op (library/rmsnorm.py:113-130, library/geglu.py:239-255,
+// torch.library.triton_op (library/rmsnorm.py:86-103, library/geglu.py:85-101,
 // library/relpos_attention.py:175-195), so that torch.compile(fullgraph=True) traces them
 // as opaque ops.  The binding owns allocation (outputs and workspaces come from the torch
 // caching allocator on the input's device), passes the current CUDA stream, and turns a

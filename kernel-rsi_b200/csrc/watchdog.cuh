@@ -29,13 +29,16 @@ constexpr unsigned kSpinLimit = 1u << 22;
 // Host readers of each translation unit's watchdog word (OR-ed by watchdog_read).
 cudaError_t watchdog_read_attn_fwd(unsigned* word, bool clear);
 cudaError_t watchdog_read_attn_bwd(unsigned* word, bool clear);
+cudaError_t watchdog_read_diag(unsigned* word, bool clear);
 
 inline cudaError_t watchdog_read(unsigned* word, bool clear) {
-  unsigned a = 0, b = 0;
+  unsigned a = 0, b = 0, c = 0;
   cudaError_t e = watchdog_read_attn_fwd(&a, clear);
   if (e != cudaSuccess) return e;
   e = watchdog_read_attn_bwd(&b, clear);
-  *word = a | b;
+  if (e != cudaSuccess) return e;
+  e = watchdog_read_diag(&c, clear);
+  *word = a | b | c;
   return e;
 }
 

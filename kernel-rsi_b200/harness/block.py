@@ -60,18 +60,64 @@ class Layer(nn.Module):
         self.wo2 = w(d, F_)
         self.pd = nn.Parameter(torch.randn(H, 2 * cfg.seq - 1, generator=gen, device=device) * 0.02)
 
+        self.attn_marks = None          # optional AttentionTimer events (forward and backward)
+
     def forward(self, x):
         cfg, ops = self.cfg, self.ops
         B, L, d = x.shape
         x2 = x.reshape(B * L, d)
         h = ops.rmsnorm(x2, self.norm1, cfg.eps)
         qkv = h @ self.wqkv.t()
+        marks = self.attn_marks
+        if marks is not None:           # fwd begin / bwd end
+            qkv = _Mark.apply(qkv, marks[0], marks[3])
         a = ops.relpos_attention(qkv, self.pd, B, L, cfg.heads, cfg.head_dim, 1.0 / math.sqrt(cfg.head_dim))
+        if marks is not None:           # fwd end / bwd begin
+            a = _Mark.apply(a, marks[1], marks[2])
         x2 = torch.addmm(x2, a, self.wo.t())        # residual add inside the GEMM (beta = 1)
         h = ops.rmsnorm(x2, self.norm2, cfg.eps)
         g = ops.geglu(h @ self.wi.t())
         x2 = torch.addmm(x2, g, self.wo2.t())
         return x2.reshape(B, L, d)
+
+
+class _Mark(torch.autograd.Function):
+    """Identity on a tensor that records one CUDA event when the forward passes it and another
+    when its gradient passes back; placed on either side of an op it brackets the op's forward and
+    backward kernels on the stream without touching the op itself."""
+
+    @staticmethod
+    def forward(ctx, x, fwd_event, bwd_event):
+        if fwd_event is not None:
+            fwd_event.record()
+        ctx.bwd_event = bwd_event
+        return x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        if ctx.bwd_event is not None:
+            ctx.bwd_event.record()
+        return g, None, None
+
+
+class AttentionTimer:
+    """CUDA events around every layer's attention forward and backward.  The events are created
+    `external`, so they keep timing when the step is captured in a CUDA graph; read them after the
+    step (or the replay) has completed."""
+
+    def __init__(self, stack: "BlockStack"):
+        mk = lambda: torch.cuda.Event(enable_timing=True, external=True)  # noqa: E731
+        self.marks = []
+        for layer in stack.layers:
+            m = (mk(), mk(), mk(), mk())     # fwd begin, fwd end, bwd begin, bwd end
+            layer.attn_marks = m
+            self.marks.append(m)
+
+    def fwd_ms(self) -> float:
+        return sum(a.elapsed_time(b) for a, b, _, _ in self.marks)
+
+    def bwd_ms(self) -> float:
+        return sum(c.elapsed_time(d) for _, _, c, d in self.marks)
 
 
 class BlockStack(nn.Module):

@@ -9,8 +9,6 @@ library/_compat.py:1-8).
 """
 import torch
 
-HAS_OP = True   # the krsi::* operators are always registered by the native extension
-
 
 def compiling() -> bool:
     return torch.compiler.is_compiling()

@@ -3,7 +3,7 @@
 The CUDA kernels live in lib/libkrsi_b200.so (C ABI, include/krsi_b200.h); lib/_krsi_torch.so
 registers the operators krsi::rmsnorm_fwd/bwd, krsi::geglu_fwd/bwd and
 krsi::relpos_attn_fwd/bwd with the schemas of the reference's triton_ops
-(library/rmsnorm.py:113-130, library/geglu.py:239-255, library/relpos_attention.py:175-195).
+(library/rmsnorm.py:86-103, library/geglu.py:85-101, library/relpos_attention.py:175-195).
 This module adds what torch.compile needs on top: fake (meta) implementations and
 register_autograd for each forward op.
 

@@ -1,9 +1,9 @@
 """GEGLU forward + backward on B200 (hand-written sm_100a CUDA) over a merged [gate | value] GEMM
 output. Use geglu(u).
 
-Drop-in for kernel-rsi's library/geglu.py: same public function (geglu.py:258-262), same
-autograd.Function contract (GEGLU, geglu.py:225-236: saves u, returns du), same operator names under
-torch.compile (krsi::geglu_fwd / krsi::geglu_bwd, geglu.py:239-255), plus reference() and selftest().
+Drop-in for kernel-rsi's library/geglu.py: same public function (geglu.py:104-108), same
+autograd.Function contract (GEGLU, geglu.py:71-82: saves u, returns du), same operator names under
+torch.compile (krsi::geglu_fwd / krsi::geglu_bwd, geglu.py:85-101), plus reference() and selftest().
 
 u: [rows, 2F]; returns gelu_tanh(u[:, :F]) * u[:, F:] with the eager bf16 rounding points. The backward
 writes d[gate | value] into one [rows, 2F] tensor, so the merged GEMM's backward reads one gradient.
@@ -42,13 +42,13 @@ def geglu(u):
 
 
 def reference(u):
-    """The torch expression this op reproduces (geglu.py:265-267)."""
+    """The torch expression this op reproduces (geglu.py:111-113)."""
     gate, value = u.chunk(2, dim=-1)
     return torch.nn.functional.gelu(gate, approximate="tanh") * value
 
 
 def selftest():
-    """Same check as the reference's selftest (geglu.py:270-274)."""
+    """Same check as the reference's selftest (geglu.py:116-120)."""
     from common import selftest_autograd  # noqa: PLC0415
 
     u = torch.randn(2048, 2 * 2816, device="cuda", dtype=torch.bfloat16)

@@ -1,8 +1,8 @@
 """RMSNorm forward + backward on B200 (hand-written sm_100a CUDA). Use rmsnorm(x2d, weight, eps).
 
-Drop-in for kernel-rsi's library/rmsnorm.py: same public function (rmsnorm.py:133-137), same
-autograd.Function contract (RMSNorm, rmsnorm.py:98-110: saves (x2d, w, rstd), returns (dx, dw, None)),
-same operator names under torch.compile (krsi::rmsnorm_fwd / krsi::rmsnorm_bwd, rmsnorm.py:113-130),
+Drop-in for kernel-rsi's library/rmsnorm.py: same public function (rmsnorm.py:106-110), same
+autograd.Function contract (RMSNorm, rmsnorm.py:71-83: saves (x2d, w, rstd), returns (dx, dw, None)),
+same operator names under torch.compile (krsi::rmsnorm_fwd / krsi::rmsnorm_bwd, rmsnorm.py:86-103),
 plus reference() and selftest().
 
 y = weight * (x * rsqrt(mean(x^2) + eps)).to(weight.dtype), rounding as in HF T5LayerNorm / LlamaRMSNorm.
@@ -46,7 +46,7 @@ def rmsnorm(x2d, w, eps):
 
 
 def reference(x2d, w, eps):
-    """The torch expression this op reproduces (rmsnorm.py:140-142): fp32 statistics, the normalised
+    """The torch expression this op reproduces (rmsnorm.py:113-115): fp32 statistics, the normalised
     row cast back to the input dtype, then scaled by the weight."""
     xf = x2d.float()
     inv = torch.rsqrt(xf.square().mean(dim=-1, keepdim=True) + eps)
@@ -54,7 +54,7 @@ def reference(x2d, w, eps):
 
 
 def selftest():
-    """Same check as the reference's selftest (rmsnorm.py:145-150): kernel vs torch, output and
+    """Same check as the reference's selftest (rmsnorm.py:118-123): kernel vs torch, output and
     gradients, eager and compiled, via the skill's tools/common.py."""
     from common import selftest_autograd  # noqa: PLC0415
 

@@ -6,7 +6,7 @@ Run in a container that has the kernel-rsi reference checkout (read-only is fine
 
 It imports the reference's library modules and records, on seeded CPU inputs in fp32:
   * the reference's Triton kernels, executed by Triton's CPU interpreter (TRITON_INTERPRET=1):
-      rmsnorm _fwd/_bwd (library/rmsnorm.py:81-95), geglu _fwd/_bwd (library/geglu.py:209-222),
+      rmsnorm _fwd/_bwd (library/rmsnorm.py:22-68), geglu _fwd/_bwd (library/geglu.py:20-68),
       relpos_attention _forward/_backward_impl (library/relpos_attention.py:132-157; D must be a
       power of two there, so D = 32 and 64);
   * the reference's eager reference() functions and their autograd gradients (fp32), including
@@ -38,7 +38,7 @@ def load_reference_module(ref: Path, name: str):
     lib = ref / "library"
     sys.path.insert(0, str(lib))
     sys.path.insert(0, str(ref / "tools"))
-    # rmsnorm.py reads the SM count of CUDA device 0 at import (rmsnorm.py:46); give it a CPU stand-in.
+    # rmsnorm.py reads the SM count of CUDA device 0 at import (rmsnorm.py:19); give it a CPU stand-in.
     real = torch.cuda.get_device_properties
 
     class _Props:
@@ -75,7 +75,7 @@ def make_rmsnorm(ref: Path):
             dx, dw = m._bwd(g, x, w, rstd, launch=m._raw)
             case.update(kernel_dx=dx, kernel_dw=dw)
         except Exception as e:  # noqa: BLE001
-            # _rms_bwd calls .to() on a Python loop index (rmsnorm.py:69), which Triton's CPU
+            # _rms_bwd calls .to() on a Python loop index (rmsnorm.py:42), which Triton's CPU
             # interpreter does not support; its gradients are pinned by reference() autograd below.
             print(f"rmsnorm[{tag}]: reference _rms_bwd not runnable in the interpreter: {type(e).__name__}")
         y_ref, (dx_ref, dw_ref) = grads_of(lambda a, b: m.reference(a, b, eps), [x, w], g)
@@ -121,7 +121,7 @@ def make_relpos(ref: Path):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("KRSI_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", required=True, help="path of the kernel-rsi checkout to run")
     a = ap.parse_args()
     ref = Path(a.reference)
     torch.backends.cuda.matmul.allow_tf32 = False

@@ -7,13 +7,15 @@ import pytest
 
 from conftest import PKG, ROOT
 
-HEADER = ROOT / "include" / "krsi_b200.h"
+HEADERS = sorted((ROOT / "include").glob("*.h"))
 
 
 def declared_functions():
-    text = HEADER.read_text()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(krsi_[a-z0-9_]+)\s*\(", text)))
+    names = set()
+    for header in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
+        names.update(re.findall(r"\b(krsi_[a-z0-9_]+)\s*\(", text))
+    return sorted(names)
 
 
 @pytest.fixture(scope="module")
@@ -22,6 +24,7 @@ def lib():
 
 
 def test_header_declares_the_hot_path():
+    assert [h.name for h in HEADERS] == ["krsi_b200.h", "krsi_b200_diag.h"]
     names = declared_functions()
     for op in ("rmsnorm_fwd", "rmsnorm_bwd", "geglu_fwd", "geglu_bwd", "relpos_attn_fwd", "relpos_attn_bwd"):
         assert f"krsi_{op}" in names

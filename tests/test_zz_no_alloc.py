@@ -1,10 +1,12 @@
 """The allocation-free RMSNorm backward (krsi_rmsnorm_bwd_noalloc) against the workspace entry point.
 
 Callers that cannot allocate device memory (a host that owns every allocation, a loop that must not
-stall on cudaMalloc) use this entry point: its scratch is a fixed array inside the library.  This test
-calls it through the C ABI twice in a row, on different inputs, and checks each result against
-krsi_rmsnorm_bwd with a caller workspace.  It lives in its own file, collected last, so a failure here
-never hides the other GPU tests."""
+stall on cudaMalloc) use this entry point: its scratch is a fixed array inside the library.  This
+test first fills that array with NaN partial sums, then calls the entry point through the C ABI
+twice in a row, on different inputs, and checks that each result is bitwise equal to
+krsi_rmsnorm_bwd with a caller workspace (same kernels, same partial-row count) and within
+tolerance of the oracle.  It lives in its own file, collected last, so a failure here never hides
+the other GPU tests."""
 import ctypes
 
 import pytest
@@ -40,17 +42,34 @@ def bwd_no_alloc(g, x, w, rstd):
     return dx, dw
 
 
+def poison_scratch():
+    """One call on non-finite inputs over a larger problem than the calls under test, so every
+    partial row they use starts out holding NaN: a row a later launch failed to write would show."""
+    x = torch.full((4096, 2048), float("nan"), device=dev)
+    w = torch.ones(2048, device=dev)
+    rstd = torch.ones(4096, device=dev)
+    dx, dw = bwd_no_alloc(x, x, w, rstd)       # 296 partial rows x 2048 columns of NaN
+    torch.cuda.synchronize()
+    assert torch.isnan(dw).all()
+
+
 @pytest.mark.parametrize("calls", [[(2048, 1152, torch.float32, 0), (300, 4096, torch.bfloat16, 1)]])
 def test_no_alloc_backward_matches_workspace_backward(calls):
+    poison_scratch()
     for rows, n, dt, seed in calls:   # two calls in a row, the second on new data and shapes
         x, w, g = (t.to(dev, dt) for t in O.rmsnorm_inputs(rows, n, torch.float32, seed=seed))
         _, rstd = torch.ops.krsi.rmsnorm_fwd(x, w, 1e-6)
         dx_ref, dw_ref = bwd_with_workspace(g, x, w, rstd)
         dx, dw = bwd_no_alloc(g, x, w, rstd)
         torch.cuda.synchronize()
+        # the same kernels with the same partial-row count: bitwise equal, not just close
+        assert torch.equal(dx, dx_ref)
+        assert torch.equal(dw, dw_ref)
+        # and both within the tolerance the other RMSNorm tests use against the oracle
+        dx_o, dw_o = O.rmsnorm_bwd(g.cpu(), x.cpu(), w.cpu(), rstd.cpu())
         tol = 1e-5 if dt == torch.float32 else 1e-2
-        assert norm_max_err(dx.float(), dx_ref.float()) <= tol
-        assert norm_max_err(dw.float(), dw_ref.float()) <= tol
+        assert norm_max_err(dx.float().cpu(), dx_o.float()) <= tol
+        assert norm_max_err(dw.float().cpu(), dw_o.float()) <= tol
 
 
 def test_no_alloc_rejects_problems_beyond_its_scratch():
