@@ -180,16 +180,19 @@ inline bool make_head_rows_map(CUtensorMap* map, const void* base, int64_t row_s
 }
 
 // 3-D fp32 view (D, S, B) of head `h` columns of a [B*S, n_heads*D] fp32 tensor, for the TMA
-// reduce-add of a [128 rows x D] tile: element (d, s, b) at base + ((b*S + s)*n_heads*D + d), the
-// caller adds h*D to the x coordinate.  Box = (D, 128, 1), no swizzle (row-major tile with a D*4-byte
-// pitch).  Rows >= S are clipped, so a ragged last block writes nothing outside its batch.
-inline bool make_rows_f32_map(CUtensorMap* map, float* base, int64_t B, int64_t S, int64_t n_heads, int64_t D) {
+// reduce-add of a [128 rows x box_cols] tile: element (d, s, b) at base + ((b*S + s)*n_heads*D + d),
+// the caller adds h*D (+ the part's first column) to the x coordinate.  Box = (box_cols, 128, 1), no
+// swizzle (row-major tile with a box_cols*4-byte pitch; box_cols * 4 a multiple of 16).  Rows >= S
+// are clipped, so a ragged last block writes nothing outside its batch.
+inline bool make_rows_f32_map(CUtensorMap* map, float* base, int64_t B, int64_t S, int64_t n_heads, int64_t D,
+                              int64_t box_cols) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
   memset(map, 0, sizeof(*map));
   cuuint64_t dims[3] = {(cuuint64_t)(n_heads * D), (cuuint64_t)S, (cuuint64_t)B};
   cuuint64_t strides[2] = {(cuuint64_t)(n_heads * D * 4), (cuuint64_t)(S * n_heads * D * 4)};
-  cuuint32_t box[3] = {(cuuint32_t)D, (cuuint32_t)kTileRows, 1};
+  if (box_cols <= 0 || box_cols > 256 || (box_cols * 4) % 16) return false;
+  cuuint32_t box[3] = {(cuuint32_t)box_cols, (cuuint32_t)kTileRows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

@@ -70,18 +70,27 @@ constexpr int kCopyBank = 16;       // distance (mod 32 floats) between the two 
 
 constexpr float kLog2e = 1.4426950408889634f;
 
+// Head dims above 80 (DP = 96, 128) do not fit dQ, dK, dV and the two score tiles in the 512 TMEM
+// columns, nor two Q/dO stages next to K, V and dS in shared memory.  For them:
+//   * the dQ tile accumulates in the dP^T columns: dQ_i is issued after dK_i has read dS_i there
+//     (the tensor pipe runs in order), and dP_{i+1} waits until dQ_i has been read out;
+//   * one Q/dO stage: the next block's S^T is issued once its loads have landed, after dK_i / dQ_i
+//     (which release the stage) instead of before them;
+//   * dQ is staged and reduce-added in two halves of D/2 columns (half the staging memory).
 template <int DP>
 struct BwdCfg {
+  static constexpr bool kWide = DP > 80;
   static constexpr uint32_t kTile = attn::Tile<DP>::kBytes;
-  static constexpr int NQS = 2;                                   // Q/dO stages
+  static constexpr int NQS = kWide ? 1 : 2;                       // Q/dO stages
+  static constexpr int kDqParts = kWide ? 2 : 1;                  // dQ staging / reduce-add parts
   static constexpr uint32_t kKOff = 0;
   static constexpr uint32_t kVOff = kKOff + kTile;
   static constexpr uint32_t kQOff = kVOff + kTile;                // stage s: Q at kQOff + s*2*kTile
   static constexpr uint32_t kDSOff = kQOff + NQS * 2 * kTile;     // dS (bf16, MN-major SW128): 2 x 16 KB
-  static constexpr uint32_t kStgOff = kDSOff + 2 * 16384;          // dQ tile staging: 128 rows x D fp32
+  static constexpr uint32_t kStgOff = kDSOff + 2 * 16384;          // dQ staging: 128 rows x D / kDqParts fp32
   // per stage: -lse[128], -delta[128] and (bias not resident) the reversed bias slab [256] with its
   // copy shifted by one element [256] placed kCopyBank (mod 32) floats after it (bank-conflict-free)
-  static constexpr uint32_t kVecOff = kStgOff + kTileRows * DP * 4;
+  static constexpr uint32_t kVecOff = kStgOff + kTileRows * (DP / kDqParts) * 4;
   static constexpr int kSlab0 = 256, kSlab1 = 256 + 256 + kCopyBank;
   static constexpr uint32_t kVecBytes = (kSlab1 + 256) * 4;
   static constexpr uint32_t kBarOff = kVecOff + NQS * kVecBytes;
@@ -90,8 +99,9 @@ struct BwdCfg {
   static constexpr uint32_t kRowOff = (kMiscOff + 16 + 15) & ~15u;   // resident rows (runtime length)
   static constexpr uint32_t kSmem = kRowOff + 1024;                  // + the 1 KB alignment slack
   static constexpr uint32_t kTmemCols = 512;
-  static constexpr uint32_t kST = 0, kDPT = 128, kDV = 256, kDK = 256 + DP, kDQ = 256 + 2 * DP;
-  static_assert(kDQ + DP <= kTmemCols, "backward TMEM plan needs DP <= 80");
+  static constexpr uint32_t kST = 0, kDPT = 128, kDV = 256, kDK = 256 + DP, kDQ = kWide ? kDPT : 256 + 2 * DP;
+  static_assert(kDK + DP <= kTmemCols && (kWide || kDQ + DP <= kTmemCols), "backward TMEM plan");
+  static_assert(kSmem <= 232448, "backward shared memory");
 };
 
 struct BwdArgs {
@@ -441,18 +451,20 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
         const uint64_t so = (uint64_t)s * kStage;
         const uint32_t acc0 = i > 0 ? 1u : 0u;
         const bool next = i + 1 < nq;
-        // dV += P^T dO, then the next block's S^T
+        auto next_s = [&]() {   // the next block's S^T, once its Q and dO have landed
+          if (!wait_all(&qdo_full[s1], ((i + 1) / NQS) & 1)) return false;
+          tc_fence_after();
+          issue_s(s1);
+          mma_commit_e(s_ready);
+          return true;
+        };
+        // dV += P^T dO, then (two stages) the next block's S^T
         if (!wait_all(p_ready, i & 1)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kBlk / 16; ++kk)
           mma_ts_e(tmem + C::kDV, tmem + C::kST + packed_col(kk), o_mn0 + so + kk * attn::kKRowStep, id_nd, kk > 0 ? 1u : acc0);
-        if (next) {
-          if (!wait_all(&qdo_full[s1], ((i + 1) / NQS) & 1)) { ok = false; break; }
-          tc_fence_after();
-          issue_s(s1);
-          mma_commit_e(s_ready);
-        }
+        if (NQS > 1 && next && !next_s()) { ok = false; break; }
         // dK += dS^T Q, dQ = dS K (dQ's TMEM columns drained), then the next block's dP^T
         if (!wait_all(ds_ready, i & 1)) { ok = false; break; }
         tc_fence_after();
@@ -467,6 +479,10 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
           mma_ss_e(tmem + C::kDQ, ds_d + kk * kDsRows, k_mn + kk * attn::kKRowStep, id_dq, kk > 0 ? 1u : 0u);
         mma_commit_e(dq_ready);
         if (next) {
+          if (NQS == 1 && !next_s()) { ok = false; break; }
+          // wide heads: dQ_i sits in the dP^T columns until the dQ warps have read it out
+          if (C::kWide && !wait_all(dq_free, i & 1)) { ok = false; break; }
+          tc_fence_after();
           issue_dp(s1);
           mma_commit_e(dp_ready);
         }
@@ -633,49 +649,58 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
     const uint32_t dq_t = tmem + lane_addr + C::kDQ;
     const bool leader = threadIdx.x == 3 * 128;
-    float* stg_row = reinterpret_cast<float*>(smem + C::kStgOff) + (size_t)r * a.D;   // pitch D floats
+    const int pc = a.D / C::kDqParts;                 // columns per staged part (a multiple of 4)
+    float* stg_row = reinterpret_cast<float*>(smem + C::kStgOff) + (size_t)r * pc;   // pitch pc floats
     bool ok = true;
-    for (int i = 0; i < nq; ++i) {
+    for (int i = 0; i < nq && ok; ++i) {
       if (!__all_sync(0xffffffffu, mbar_wait_bounded(dq_ready, i & 1, abort_flag, a.spin_limit))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      // the staging tile is free once the previous reduce-add has read it (mbarriers, not bar.sync,
-      // so that every wait stays bounded)
-      if (leader) {
-        bulk_wait_read_all();
-        mbar_arrive(stg_free);
-      }
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(stg_free, i & 1, abort_flag, a.spin_limit))) {
-        ok = false;
-        break;
-      }
 #pragma unroll
-      for (int c = 0; c < DP; c += 16) {
-        uint32_t u[16];
-        tmem_ld16(dq_t + c, u);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 16; e += 4)
-          if (c + e < a.D)
-            *reinterpret_cast<uint4*>(stg_row + c + e) = make_uint4(u[e], u[e + 1], u[e + 2], u[e + 3]);
-      }
-      tc_fence_before();
-      mbar_arrive(dq_free);
-      fence_async_shared();   // staging writes -> visible to the TMA unit
-      mbar_arrive(stg_full);
-      if (leader) {
-        if (!mbar_wait_bounded(stg_full, i & 1, abort_flag, a.spin_limit)) {
-          ok = false;
-        } else {
-          tma_reduce_add_3d(&dqmap, smem + C::kStgOff, h * a.D, i * kBlk, b);
-          bulk_commit_group();
+      for (int part = 0; part < C::kDqParts; ++part) {
+        const uint32_t ph = (uint32_t)(i * C::kDqParts + part) & 1u;
+        // the staging tile is free once the previous reduce-add has read it (mbarriers, not
+        // bar.sync, so that every wait stays bounded)
+        if (leader) {
+          bulk_wait_read_all();
+          mbar_arrive(stg_free);
         }
-      }
-      if (!__all_sync(0xffffffffu, ok)) {   // the leader's failure ends its whole warp
-        ok = false;
-        break;
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(stg_free, ph, abort_flag, a.spin_limit))) {
+          ok = false;
+          break;
+        }
+        const int lo = part * pc, hi = lo + pc;
+#pragma unroll
+        for (int c = 0; c < DP; c += 16) {
+          if (c + 16 <= lo || c >= hi) continue;   // warp-uniform
+          uint32_t u[16];
+          tmem_ld16(dq_t + c, u);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; e += 4)
+            if (c + e >= lo && c + e < hi)
+              *reinterpret_cast<uint4*>(stg_row + c + e - lo) = make_uint4(u[e], u[e + 1], u[e + 2], u[e + 3]);
+        }
+        if (part == C::kDqParts - 1) {   // every column of this dQ tile has left TMEM
+          tc_fence_before();
+          mbar_arrive(dq_free);
+        }
+        fence_async_shared();   // staging writes -> visible to the TMA unit
+        mbar_arrive(stg_full);
+        if (leader) {
+          if (!mbar_wait_bounded(stg_full, ph, abort_flag, a.spin_limit)) {
+            ok = false;
+          } else {
+            tma_reduce_add_3d(&dqmap, smem + C::kStgOff, h * a.D + lo, i * kBlk, b);
+            bulk_commit_group();
+          }
+        }
+        if (!__all_sync(0xffffffffu, ok)) {   // the leader's failure ends its whole warp
+          ok = false;
+          break;
+        }
       }
     }
     if (leader) bulk_wait_all();
@@ -858,6 +883,8 @@ int dispatch_dp(int DP, const CUtensorMap& qm, const CUtensorMap& om, const CUte
     case 32: return launch_bwd<32, F16>(qm, om, dqm, kvm, a, dout, out32, dpd, s);
     case 64: return launch_bwd<64, F16>(qm, om, dqm, kvm, a, dout, out32, dpd, s);
     case 80: return launch_bwd<80, F16>(qm, om, dqm, kvm, a, dout, out32, dpd, s);
+    case 96: return launch_bwd<96, F16>(qm, om, dqm, kvm, a, dout, out32, dpd, s);
+    case 128: return launch_bwd<128, F16>(qm, om, dqm, kvm, a, dout, out32, dpd, s);
     default: return KRSI_ERR_UNSUPPORTED;
   }
 }
@@ -887,7 +914,7 @@ extern "C" int krsi_relpos_attn_bwd(const void* dout, const void* qkv, int64_t q
   KRSI_CHECK_ARG(dout && qkv && pd && out32 && lse && dqkv);
   if (dtype != KRSI_BF16 && dtype != KRSI_F16) return KRSI_ERR_UNSUPPORTED;
   const int DP = attn_padded_dim(D);
-  if (DP < 0 || DP > 80) return KRSI_ERR_UNSUPPORTED;
+  if (DP < 0) return KRSI_ERR_UNSUPPORTED;
   KRSI_CHECK_ARG(qkv_row_stride >= 3 * H * D && dqkv_row_stride >= 3 * H * D);
   if (qkv_row_stride % 8 || dqkv_row_stride % 8 || !aligned16(qkv) || !aligned16(dqkv) || !aligned16(dout) ||
       !aligned16(out32))
@@ -900,7 +927,7 @@ extern "C" int krsi_relpos_attn_bwd(const void* dout, const void* qkv, int64_t q
   const bool f16 = dtype == KRSI_F16;
   if (!attn::make_head_map(&qm, qkv, qkv_row_stride, B, S, 3 * H, D, f16) ||
       !attn::make_head_map(&om, dout, H * D, B, S, H, D, f16) ||
-      !attn::make_rows_f32_map(&dqm, reinterpret_cast<float*>(w + ws.dq), B, S, H, D) ||
+      !attn::make_rows_f32_map(&dqm, reinterpret_cast<float*>(w + ws.dq), B, S, H, D, DP > 80 ? D / 2 : D) ||
       !attn::make_head_rows_map(&kvm, dqkv, dqkv_row_stride, B, S, 3 * H, D, f16))
     return KRSI_ERR_CUDA;
   BwdArgs a{pd,

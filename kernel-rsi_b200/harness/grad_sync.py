@@ -2,10 +2,14 @@
 
 Each rank runs forward+backward on its own batch shard; the only collective is one SUM all-reduce
 per bucket of weight gradients (the loss is pre-scaled by 1/world, so the sum is the global-batch
-gradient).  Buckets are the layers, in reverse order: a layer's bucket is launched asynchronously
-(NCCL's own stream) the moment autograd has accumulated its last gradient, so communication of
-layer l overlaps the backward of layers l-1 ... 0.  Gradients live in one flat buffer per layer
-and dtype (param.grad are views into it), so no packing copies are needed.
+gradient).  Gradients live in one flat buffer per bucket (param.grad are views into it), so no
+packing copies are needed, and a bucket is launched asynchronously (NCCL's own stream) the moment
+autograd has accumulated its last gradient, so its communication overlaps the rest of the backward.
+
+Buckets: the bf16 weights of `layers_per_bucket` consecutive layers (backward order: the last
+layers' bucket fills first), and the small fp32 tensors of every layer (the relative-position
+tables, 131 KB a layer) in one bucket of their own, launched when the first layer's table gradient
+lands near the end of the backward (one collective instead of one latency-bound call per layer).
 """
 from __future__ import annotations
 
@@ -16,27 +20,41 @@ import torch.distributed as dist
 
 
 class LayerBucketAllReduce:
-    def __init__(self, layers, group=None):
+    def __init__(self, layers, group=None, layers_per_bucket: int = 1, small_bytes: int = 1 << 20):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
-        self.buckets = []       # (layer index, dtype, flat buffer, [params])
+        self.buckets = []       # (bucket key, dtype, flat buffer, [params])
         self.pending = defaultdict(int)
         self.handles = []
         self.param_bucket = {}
+        n = len(layers)
+        groups = defaultdict(list)      # key -> params, in layer order
+        per_layer_bytes = defaultdict(int)   # the largest layer's share of each dtype
         for li, layer in enumerate(layers):
-            by_dtype = defaultdict(list)
+            by_dtype = defaultdict(int)
             for p in layer.parameters():
                 if p.requires_grad:
-                    by_dtype[p.dtype].append(p)
-            for dt, params in by_dtype.items():
-                n = sum(p.numel() for p in params)
-                flat = torch.zeros(n, dtype=dt, device=params[0].device)
-                off = 0
-                for p in params:
-                    p.grad = flat[off: off + p.numel()].view_as(p)
-                    off += p.numel()
-                    self.param_bucket[p] = len(self.buckets)
-                self.buckets.append((li, dt, flat, params))
+                    by_dtype[p.dtype] += p.numel() * p.element_size()
+            for dt, b in by_dtype.items():
+                per_layer_bytes[dt] = max(per_layer_bytes[dt], b)
+        for li, layer in enumerate(layers):
+            for p in layer.parameters():
+                if not p.requires_grad:
+                    continue
+                if per_layer_bytes[p.dtype] < small_bytes:
+                    key = ("all", p.dtype)                              # one bucket for all layers
+                else:
+                    key = ((n - 1 - li) // max(1, layers_per_bucket), p.dtype)
+                groups[key].append(p)
+        for key, params in groups.items():
+            total = sum(p.numel() for p in params)
+            flat = torch.zeros(total, dtype=params[0].dtype, device=params[0].device)
+            off = 0
+            for p in params:
+                p.grad = flat[off: off + p.numel()].view_as(p)
+                off += p.numel()
+                self.param_bucket[p] = len(self.buckets)
+            self.buckets.append((key, params[0].dtype, flat, params))
         self.hooks = [p.register_post_accumulate_grad_hook(self._on_grad) for p in self.param_bucket]
 
     @property

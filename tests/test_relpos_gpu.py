@@ -121,6 +121,12 @@ def attn_bwd_check(B, S, H, D, dtype=torch.bfloat16, seed=0, tol=1e-2):
     errs["dpd"] = norm_max_err(dpd, dpd_ref)
     assert torch.isfinite(dqkv.float()).all() and torch.isfinite(dpd).all()
     assert all(e <= tol for e in errs.values()), errs
+    # and end to end from the oracle's own forward (out32, lse), so that a forward/backward
+    # convention shared by both kernels cannot hide
+    _, o32_o, lse_o = O.relpos_attn_fwd(qd, pdd, B, S, H, D, scale)
+    dq_o, dpd_o = O.relpos_attn_bwd(dod, qd, pdd, o32_o, lse_o, B, S, H, D, scale)
+    e2e = {"dqkv": norm_max_err(dqkv.float(), dq_o.double()), "dpd": norm_max_err(dpd, dpd_o)}
+    assert all(e <= tol for e in e2e.values()), e2e
     return dqkv, dpd
 
 
@@ -134,12 +140,17 @@ def attn_bwd_check(B, S, H, D, dtype=torch.bfloat16, seed=0, tol=1e-2):
     (1, 520, 2, 32),
     (1, 300, 2, 56),     # D % 16 == 8 with 64 padded columns: -lse / -delta folded into the MMAs
     (1, 200, 1, 24),
+    (1, 256, 1, 96),     # wide heads (D > 80): dQ in the dP^T columns, one Q/dO stage, dQ in halves
+    (1, 300, 2, 128),
+    (2, 200, 2, 120),    # wide and D % 16 == 8 (folded lse / delta)
+    (1, 384, 2, 88),
+    (1, 1, 1, 128),
 ])
 def test_bwd_small_shapes(B, S, H, D):
     attn_bwd_check(B, S, H, D, seed=7 * S + D)
 
 
-@pytest.mark.parametrize("D", [72, 64])
+@pytest.mark.parametrize("D", [72, 64, 128])
 def test_bwd_streamed_bias(D):
     """S = 4608: the reversed bias window no longer fits beside the tiles, so each query block's bias
     slab is streamed with its Q/dO stage (folded and unfolded lse/delta)."""
@@ -196,6 +207,25 @@ def test_reference_selftest_criterion(S):
 
     B, H, D = 2, 16, 72
     g = torch.Generator().manual_seed(S)
+    qkv = (0.6 * torch.randn(B * S, 3 * H * D, generator=g)).to(torch.bfloat16).to(dev)
+    pd = torch.randn(H, 2 * S - 1, generator=g).to(dev)
+    cot = (torch.randn(B * S, H * D, generator=g) * 1e-2).to(dev)
+    res, ref32, cand = reference_compare(lambda q, p: ra.relpos_attention(q, p, B, S, H, D, 1.0),
+                                         lambda q, p: O.relpos_reference(q, p, B, S, H, D, 1.0), [qkv, pd], cot)
+    assert res["pass"], res
+    for r, c in zip(ref32, cand):
+        assert norm_max_err(c, r) <= 1e-2
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_reference_selftest_shape(D):
+    """The reference's selftest shape and scale (relpos_attention.py:215-222: B=4, S=512, H=16, scale 1,
+    qkv ~ 0.6 N(0,1), pd ~ N(0,1)) at its own head dim 64 and at 128, the largest it supports, under
+    its compare() criterion."""
+    import relpos_attention as ra
+
+    B, S, H = 4, 512, 16
+    g = torch.Generator().manual_seed(D)
     qkv = (0.6 * torch.randn(B * S, 3 * H * D, generator=g)).to(torch.bfloat16).to(dev)
     pd = torch.randn(H, 2 * S - 1, generator=g).to(dev)
     cot = (torch.randn(B * S, H * D, generator=g) * 1e-2).to(dev)
