@@ -2,7 +2,9 @@
 
 Each layer:  x -> RMSNorm -> fused q|k|v GEMM -> relpos attention (H heads of D) -> out GEMM + x
                 -> RMSNorm -> merged gate|value GEMM (d -> 2F) -> GEGLU -> down GEMM (F -> d) + x
-(the residual adds ride in the out and down GEMMs: addmm with beta = 1)
+(the residual adds ride in the out and down GEMMs: addmm with beta = 1; the weight gradients of
+the four GEMMs are written straight into the all-reduce buckets when a LayerBucketAllReduce owns
+them)
 The attention, RMSNorm and GEGLU calls are the kernel-rsi library functions (relpos_attention(),
 rmsnorm(), geglu(), with the reference's signatures); the GEMMs are torch matmuls (cuBLAS).  loss =
 mean(out.float()^2).  Weights are bf16 ~ N(0, 0.02) (RMSNorm weights 1 + N(0, 0.02)), the per-layer
@@ -14,10 +16,61 @@ CPU tests of the distributed harness, on any stand-in with the same signatures.
 from __future__ import annotations
 
 import math
+import weakref
 from dataclasses import dataclass
 
 import torch
 from torch import nn
+
+# id(weight) -> (weak weight, weak bucket owner): the gradient all-reduce that owns the weight's
+# .grad slot (see _Linear).  Keyed by identity and held weakly, so copies of a model (deepcopy makes
+# new Parameters) and dropped reducers leave no trace.
+_GRAD_SINKS: dict = {}
+
+
+def set_grad_sink(w: torch.Tensor, owner) -> None:
+    _GRAD_SINKS[id(w)] = (weakref.ref(w), weakref.ref(owner))
+
+
+def clear_grad_sink(w: torch.Tensor, owner) -> None:
+    if grad_sink(w) is owner:
+        del _GRAD_SINKS[id(w)]
+
+
+def grad_sink(w: torch.Tensor):
+    entry = _GRAD_SINKS.get(id(w))
+    if entry is None or entry[0]() is not w:
+        return None
+    return entry[1]()
+
+
+class _Linear(torch.autograd.Function):
+    """y = x @ w^T (+ res, with beta = 1).  When the weight's gradient lives in a bucket of a
+    gradient all-reduce (grad_sink(w), set by LayerBucketAllReduce), the backward writes
+    dW = g^T x straight into the weight's .grad view of the bucket (cuBLAS with `out=`) and tells
+    the bucket it is ready, instead of handing dW to autograd, which would add it onto a zeroed
+    bucket: a zero pass and a read-modify-write of every weight gradient each step."""
+
+    @staticmethod
+    def forward(ctx, x, w, res):
+        ctx.save_for_backward(x, w)
+        ctx.w = w
+        ctx.has_res = res is not None
+        return torch.addmm(res, x, w.t()) if res is not None else x @ w.t()
+
+    @staticmethod
+    def backward(ctx, g):
+        x, w = ctx.saved_tensors
+        gx = g @ w if ctx.needs_input_grad[0] else None
+        gw = None
+        if ctx.needs_input_grad[1]:
+            sink = grad_sink(ctx.w)
+            if sink is not None and ctx.w.grad is not None:
+                torch.mm(g.t(), x, out=ctx.w.grad)
+                sink.mark_ready(ctx.w)
+            else:
+                gw = g.t() @ x
+        return gx, gw, (g if ctx.has_res else None)
 
 
 @dataclass
@@ -67,18 +120,22 @@ class Layer(nn.Module):
         B, L, d = x.shape
         x2 = x.reshape(B * L, d)
         h = ops.rmsnorm(x2, self.norm1, cfg.eps)
-        qkv = h @ self.wqkv.t()
+        qkv = _Linear.apply(h, self.wqkv, None)
         marks = self.attn_marks
         if marks is not None:           # fwd begin / bwd end
             qkv = _Mark.apply(qkv, marks[0], marks[3])
         a = ops.relpos_attention(qkv, self.pd, B, L, cfg.heads, cfg.head_dim, 1.0 / math.sqrt(cfg.head_dim))
         if marks is not None:           # fwd end / bwd begin
             a = _Mark.apply(a, marks[1], marks[2])
-        x2 = torch.addmm(x2, a, self.wo.t())        # residual add inside the GEMM (beta = 1)
+        x2 = _Linear.apply(a, self.wo, x2)          # residual add inside the GEMM (beta = 1)
         h = ops.rmsnorm(x2, self.norm2, cfg.eps)
-        g = ops.geglu(h @ self.wi.t())
-        x2 = torch.addmm(x2, g, self.wo2.t())
+        g = ops.geglu(_Linear.apply(h, self.wi, None))
+        x2 = _Linear.apply(g, self.wo2, x2)
         return x2.reshape(B, L, d)
+
+    def linear_weights(self):
+        """The weights used through _Linear (their gradients can be written into a bucket)."""
+        return [self.wqkv, self.wo, self.wi, self.wo2]
 
 
 class _Mark(torch.autograd.Function):

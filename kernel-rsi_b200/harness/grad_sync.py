@@ -25,6 +25,7 @@ class LayerBucketAllReduce:
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.buckets = []       # (bucket key, dtype, flat buffer, [params])
         self.pending = defaultdict(int)
+        self.ready = set()
         self.handles = []
         self.param_bucket = {}
         n = len(layers)
@@ -37,7 +38,10 @@ class LayerBucketAllReduce:
                     by_dtype[p.dtype] += p.numel() * p.element_size()
             for dt, b in by_dtype.items():
                 per_layer_bytes[dt] = max(per_layer_bytes[dt], b)
+        direct = set()          # weights whose GEMM backward writes the bucket slot itself
         for li, layer in enumerate(layers):
+            lw = getattr(layer, "linear_weights", None)
+            direct.update(lw() if lw is not None else [])
             for p in layer.parameters():
                 if not p.requires_grad:
                     continue
@@ -46,7 +50,11 @@ class LayerBucketAllReduce:
                 else:
                     key = ((n - 1 - li) // max(1, layers_per_bucket), p.dtype)
                 groups[key].append(p)
+        from .block import set_grad_sink
+
+        self.zero_tails = []    # the accumulated (not directly written) part of each bucket
         for key, params in groups.items():
+            params = [p for p in params if p in direct] + [p for p in params if p not in direct]
             total = sum(p.numel() for p in params)
             flat = torch.zeros(total, dtype=params[0].dtype, device=params[0].device)
             off = 0
@@ -54,20 +62,36 @@ class LayerBucketAllReduce:
                 p.grad = flat[off: off + p.numel()].view_as(p)
                 off += p.numel()
                 self.param_bucket[p] = len(self.buckets)
+                if p in direct:
+                    set_grad_sink(p, self)
+            n_direct = sum(p.numel() for p in params if p in direct)
+            if n_direct < total:
+                self.zero_tails.append(flat[n_direct:])
             self.buckets.append((key, params[0].dtype, flat, params))
-        self.hooks = [p.register_post_accumulate_grad_hook(self._on_grad) for p in self.param_bucket]
+        # direct weights normally bypass autograd's accumulation (so their hook never fires); if one
+        # is ever handed to autograd instead, its hook still marks it ready exactly once
+        self.hooks = [p.register_post_accumulate_grad_hook(self.mark_ready) for p in self.param_bucket]
 
     @property
     def bytes(self) -> int:
         return sum(f.numel() * f.element_size() for _, _, f, _ in self.buckets)
 
     def zero_grad(self):
-        for _, _, flat, _ in self.buckets:
-            flat.zero_()
+        """Zero the slots that autograd accumulates into; the GEMM weights' slots are overwritten
+        by their backward."""
+        for tail in self.zero_tails:
+            tail.zero_()
         self.pending.clear()
+        self.ready.clear()
         self.handles.clear()
 
-    def _on_grad(self, p):
+    def mark_ready(self, p):
+        """Gradient of p is final for this step; launches its bucket's all-reduce when complete.
+        Repeated calls for one parameter in a step count once (autograd may still run the
+        accumulate hook of a weight whose GEMM backward wrote its gradient itself)."""
+        if id(p) in self.ready:
+            return
+        self.ready.add(id(p))
         bi = self.param_bucket[p]
         self.pending[bi] += 1
         _, _, flat, params = self.buckets[bi]
@@ -81,8 +105,12 @@ class LayerBucketAllReduce:
         self.handles.clear()
 
     def remove(self):
+        from .block import clear_grad_sink
+
         for h in self.hooks:
             h.remove()
+        for p in self.param_bucket:
+            clear_grad_sink(p, self)
 
 
 def shard_batch(x: torch.Tensor, rank: int, world: int) -> torch.Tensor:

@@ -145,6 +145,26 @@ def test_bucket_plan():
     assert red.bytes == sum(p.numel() * p.element_size() for p in model.parameters())
 
 
+def test_gemm_gradients_written_into_buckets_match_autograd():
+    """The bucket-owned weights get dW written by their GEMM backward; the same model without a
+    reducer gets plain autograd gradients: equal, and the reducer's accumulated tails are zeroed."""
+    import copy
+
+    from harness.block import loss_fn
+    from harness.grad_sync import LayerBucketAllReduce, train_step
+    cfg = tiny_cfg()
+    model = make_model(cfg)
+    plain = copy.deepcopy(model)
+    reducer = LayerBucketAllReduce(model.layers, small_bytes=0)
+    x = global_batch(cfg)
+    for _ in range(2):                      # a second step must not accumulate onto the first
+        train_step(model, x, reducer, 1, loss_fn)
+    loss_fn(plain(x)).backward()
+    for (n, a), (_, b) in zip(model.named_parameters(), plain.named_parameters()):
+        torch.testing.assert_close(a.grad, b.grad, rtol=1e-5, atol=1e-7, msg=n)
+    assert reducer.zero_tails and sum(t.numel() for t in reducer.zero_tails) < reducer.bytes // 4
+
+
 def test_dead_rank_raises_instead_of_hanging():
     res = run_ranks(2, "die")
     assert res[1][0] == "error" and "planted" in res[1][1]
