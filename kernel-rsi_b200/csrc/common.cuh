@@ -7,6 +7,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/krsi_b200.h"
 
 #define KRSI_CHECK_ARG(cond)                    \
@@ -33,6 +35,37 @@ void krsi_set_last_cuda_error(cudaError_t e);
 namespace krsi {
 
 constexpr int kNumSMsB200 = 148;
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// Every kernel of this library is launched with programmatic stream serialisation, so the next
+// kernel in the stream is launched (and its CTAs placed on SMs as ours finish) while ours still
+// runs, instead of after a launch gap.  The rule that keeps this safe: every kernel calls
+// pdl_wait() before its first global-memory access, in every thread, unconditionally: it returns
+// once the preceding kernel in the stream has completed and its writes are visible (at once if that
+// kernel was launched normally and has finished), so a chain of such kernels stays in stream order.
+// pdl_launch_dependents() right after it lets the next kernel launch early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_enter() {
+  pdl_wait();
+  pdl_launch_dependents();
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -56,6 +56,7 @@ template <int DT>
 __global__ void __launch_bounds__(256)
 geglu_fwd_vec(const typename Elem<DT>::T* __restrict__ u, typename Elem<DT>::T* __restrict__ out,
               uint32_t items, uint32_t FV) {
+  pdl_enter();
   using E = Elem<DT>;
   using T = typename E::T;
   constexpr int VEC = Vec16<T>::N;
@@ -86,6 +87,7 @@ template <int DT>
 __global__ void __launch_bounds__(256)
 geglu_bwd_vec(const typename Elem<DT>::T* __restrict__ g, const typename Elem<DT>::T* __restrict__ u,
               typename Elem<DT>::T* __restrict__ du, uint32_t items, uint32_t FV) {
+  pdl_enter();
   using E = Elem<DT>;
   using T = typename E::T;
   constexpr int VEC = Vec16<T>::N;
@@ -114,6 +116,7 @@ template <int DT>
 __global__ void __launch_bounds__(256)
 geglu_fwd_scalar(const typename Elem<DT>::T* __restrict__ u, typename Elem<DT>::T* __restrict__ out,
                  int64_t items, int64_t F) {
+  pdl_enter();
   using E = Elem<DT>;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < items;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -127,6 +130,7 @@ template <int DT>
 __global__ void __launch_bounds__(256)
 geglu_bwd_scalar(const typename Elem<DT>::T* __restrict__ g, const typename Elem<DT>::T* __restrict__ u,
                  typename Elem<DT>::T* __restrict__ du, int64_t items, int64_t F) {
+  pdl_enter();
   using E = Elem<DT>;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < items;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -154,12 +158,12 @@ int fwd_t(const void* u, void* out, int64_t rows, int64_t F, cudaStream_t s) {
   const int64_t items = rows * F;
   if (F % VEC == 0 && aligned16(u) && aligned16(out) && items / VEC < 0xffffffffLL) {
     const int64_t vitems = items / VEC;
-    geglu_fwd_vec<DT><<<grid_for(vitems, 512), 256, 0, s>>>((const T*)u, (T*)out, (uint32_t)vitems,
-                                                            (uint32_t)(F / VEC));
+    KRSI_CUDA_TRY(launch_pdl(geglu_fwd_vec<DT>, dim3(grid_for(vitems, 512)), dim3(256), 0, s, (const T*)u, (T*)out,
+                             (uint32_t)vitems, (uint32_t)(F / VEC)));
   } else {
-    geglu_fwd_scalar<DT><<<grid_for(items, 256), 256, 0, s>>>((const T*)u, (T*)out, items, F);
+    KRSI_CUDA_TRY(launch_pdl(geglu_fwd_scalar<DT>, dim3(grid_for(items, 256)), dim3(256), 0, s, (const T*)u, (T*)out,
+                             items, F));
   }
-  KRSI_LAUNCH_CHECK();
   return KRSI_OK;
 }
 
@@ -170,12 +174,12 @@ int bwd_t(const void* g, const void* u, void* du, int64_t rows, int64_t F, cudaS
   const int64_t items = rows * F;
   if (F % VEC == 0 && aligned16(u) && aligned16(du) && aligned16(g) && items / VEC < 0xffffffffLL) {
     const int64_t vitems = items / VEC;
-    geglu_bwd_vec<DT><<<grid_for(vitems, 256), 256, 0, s>>>((const T*)g, (const T*)u, (T*)du,
-                                                            (uint32_t)vitems, (uint32_t)(F / VEC));
+    KRSI_CUDA_TRY(launch_pdl(geglu_bwd_vec<DT>, dim3(grid_for(vitems, 256)), dim3(256), 0, s, (const T*)g, (const T*)u,
+                             (T*)du, (uint32_t)vitems, (uint32_t)(F / VEC)));
   } else {
-    geglu_bwd_scalar<DT><<<grid_for(items, 256), 256, 0, s>>>((const T*)g, (const T*)u, (T*)du, items, F);
+    KRSI_CUDA_TRY(launch_pdl(geglu_bwd_scalar<DT>, dim3(grid_for(items, 256)), dim3(256), 0, s, (const T*)g,
+                             (const T*)u, (T*)du, items, F));
   }
-  KRSI_LAUNCH_CHECK();
   return KRSI_OK;
 }
 

@@ -158,6 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap omap,
                        const __grid_constant__ CUtensorMap dqmap, const __grid_constant__ CUtensorMap kvmap,
                        const BwdArgs a) {
+  pdl_enter();   // before any global access and before claiming TMEM
   using C = BwdCfg<DP>;
   constexpr int NQS = C::NQS;
   extern __shared__ uint8_t smem_raw[];
@@ -721,6 +722,7 @@ template <bool F16>
 __global__ void __launch_bounds__(32 * 16)
 relpos_bwd_prep_kernel(const void* __restrict__ dout, const float* __restrict__ out32, float* __restrict__ delta,
                        float* __restrict__ dq_acc, int64_t pairs, int S, int H, int cph) {
+  pdl_enter();
   using T = typename std::conditional<F16, __half, __nv_bfloat16>::type;
   __shared__ float part[32 * 16];
   const int64_t p0 = (int64_t)blockIdx.x * 32;
@@ -757,6 +759,7 @@ template <bool F16>
 __global__ void __launch_bounds__(256)
 relpos_bwd_dq_kernel(const float* __restrict__ dq_acc, void* __restrict__ dqkv, int64_t dqkv_stride, int64_t rows,
                      int HD, float scale) {
+  pdl_enter();
   using T = typename std::conditional<F16, __half, __nv_bfloat16>::type;
   const int64_t per_row = HD / 8;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -786,6 +789,7 @@ constexpr int kDiagChunks = 8;
 __host__ __device__ inline int diag_chunks(int B) { return B < kDiagChunks ? B : kDiagChunks; }
 __global__ void __launch_bounds__(kDiagThreads)
 relpos_bwd_dpd_diag_kernel(const float* __restrict__ part, float* __restrict__ rows, int B, int H, int nb) {
+  pdl_enter();
   __shared__ float acc[kDiagThreads];
   const int d = (int)blockIdx.x - (nb - 1), h = blockIdx.y, c = blockIdx.z, nc = diag_chunks(B);
   const int kb_lo = d > 0 ? d : 0, kb_hi = d > 0 ? nb : nb + d;   // qb = kb - d in [0, nb)
@@ -814,6 +818,7 @@ relpos_bwd_dpd_diag_kernel(const float* __restrict__ part, float* __restrict__ r
 // over the batch chunks in chunk order.
 __global__ void __launch_bounds__(256)
 relpos_bwd_dpd_kernel(const float* __restrict__ rows, float* __restrict__ dpd, int S, int H, int nb, int nc) {
+  pdl_enter();
   const int h = blockIdx.y;
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= 2 * S - 1) return;
@@ -850,9 +855,9 @@ int launch_bwd(const CUtensorMap& qm, const CUtensorMap& om, const CUtensorMap& 
                const BwdArgs& a, const void* dout, const float* out32, float* dpd, cudaStream_t stream) {
   using C = BwdCfg<DP>;
   const int64_t tokens_heads = (int64_t)a.B * a.S * a.H;
-  relpos_bwd_prep_kernel<F16><<<(unsigned)((tokens_heads + 31) / 32), 32 * (a.D / 8), 0, stream>>>(
-      dout, out32, const_cast<float*>(a.delta), a.dq_acc, tokens_heads, a.S, a.H, a.D / 8);
-  KRSI_LAUNCH_CHECK();
+  KRSI_CUDA_TRY(launch_pdl(relpos_bwd_prep_kernel<F16>, dim3((unsigned)((tokens_heads + 31) / 32)),
+                           dim3(32 * (a.D / 8)), 0, stream, dout, out32, const_cast<float*>(a.delta), a.dq_acc,
+                           tokens_heads, a.S, a.H, a.D / 8));
   const size_t res_smem = C::kSmem + (size_t)rows_bytes(a.S);
   const bool res = res_smem <= 232448;   // 227 KB per CTA on sm_100
   const bool fold = a.D % 16 == 8;       // padding columns D..D+2 free for -lse / -delta
@@ -860,19 +865,15 @@ int launch_bwd(const CUtensorMap& qm, const CUtensorMap& om, const CUtensorMap& 
                   : (fold ? relpos_bwd_main_kernel<DP, F16, false, true> : relpos_bwd_main_kernel<DP, F16, false, false>);
   const size_t smem = res ? res_smem : C::kSmem;
   KRSI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  kern<<<dim3(a.n_blk, a.B * a.H), kThreads, smem, stream>>>(qm, om, dqm, kvm, a);
-  KRSI_LAUNCH_CHECK();
+  KRSI_CUDA_TRY(launch_pdl(kern, dim3(a.n_blk, a.B * a.H), dim3(kThreads), smem, stream, qm, om, dqm, kvm, a));
   const int64_t rows = (int64_t)a.B * a.S;
   const int64_t items = rows * (a.H * a.D / 8);
-  relpos_bwd_dq_kernel<F16><<<(unsigned)((items + 255) / 256), 256, 0, stream>>>(a.dq_acc, a.dqkv, a.dqkv_stride,
-                                                                                  rows, a.H * a.D, a.scale);
-  KRSI_LAUNCH_CHECK();
-  relpos_bwd_dpd_diag_kernel<<<dim3(2 * a.n_blk - 1, a.H, diag_chunks(a.B)), kDiagThreads, 0, stream>>>(
-      a.dbias_part, a.dpd_rows, a.B, a.H, a.n_blk);
-  KRSI_LAUNCH_CHECK();
-  relpos_bwd_dpd_kernel<<<dim3((2 * a.S - 1 + 255) / 256, a.H), 256, 0, stream>>>(a.dpd_rows, dpd, a.S, a.H, a.n_blk,
-                                                                                  diag_chunks(a.B));
-  KRSI_LAUNCH_CHECK();
+  KRSI_CUDA_TRY(launch_pdl(relpos_bwd_dq_kernel<F16>, dim3((unsigned)((items + 255) / 256)), dim3(256), 0, stream,
+                           (const float*)a.dq_acc, a.dqkv, a.dqkv_stride, rows, a.H * a.D, a.scale));
+  KRSI_CUDA_TRY(launch_pdl(relpos_bwd_dpd_diag_kernel, dim3(2 * a.n_blk - 1, a.H, diag_chunks(a.B)),
+                           dim3(kDiagThreads), 0, stream, (const float*)a.dbias_part, a.dpd_rows, a.B, a.H, a.n_blk));
+  KRSI_CUDA_TRY(launch_pdl(relpos_bwd_dpd_kernel, dim3((2 * a.S - 1 + 255) / 256, a.H), dim3(256), 0, stream,
+                           (const float*)a.dpd_rows, dpd, a.S, a.H, a.n_blk, diag_chunks(a.B)));
   return KRSI_OK;
 }
 

@@ -125,6 +125,7 @@ __device__ __forceinline__ void fill_shifted(float* dst, int n, int off, const f
 template <int DP, bool F16, bool RES>
 __global__ void __launch_bounds__(kThreads, 1)
 relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
+  pdl_enter();   // before any global access and before claiming TMEM
   using C = FwdCfg<DP>;
   constexpr int NS = C::NS;
   extern __shared__ uint8_t smem_raw[];
@@ -595,8 +596,7 @@ int launch_fwd(const CUtensorMap& tmap, const FwdArgs& a, cudaStream_t stream) {
   KRSI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int64_t items = (int64_t)a.B * a.H * a.n_qp;   // persistent: at most one CTA per SM
   const int grid = (int)(items < device_sm_count() ? items : device_sm_count());
-  kern<<<grid, kThreads, smem, stream>>>(tmap, a);
-  KRSI_LAUNCH_CHECK();
+  KRSI_CUDA_TRY(launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, tmap, a));
   return KRSI_OK;
 }
 

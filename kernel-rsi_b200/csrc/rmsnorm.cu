@@ -69,6 +69,7 @@ template <int XT, int WT, int TPR, int VEC, int NCH>
 __global__ void __launch_bounds__(RowCfg<TPR>::kThreads)
 rms_fwd_kernel(const typename Elem<XT>::T* __restrict__ x, const typename Elem<WT>::T* __restrict__ w,
                typename Elem<XT>::T* __restrict__ y, float* __restrict__ rstd, int64_t rows, int n, float eps) {
+  pdl_enter();
   using WE = Elem<WT>;
   __shared__ float red[32];
   const int t = threadIdx.x % TPR;
@@ -142,6 +143,7 @@ __global__ void __launch_bounds__(RowCfg<TPR>::kThreads, kBwdMinBlocks<TPR, VEC,
 rms_bwd_kernel(const typename Elem<XT>::T* __restrict__ g, const typename Elem<XT>::T* __restrict__ x,
                const typename Elem<WT>::T* __restrict__ w, const float* __restrict__ rstd,
                typename Elem<XT>::T* __restrict__ dx, float* __restrict__ dw_part, int64_t rows, int n) {
+  pdl_enter();
   using WE = Elem<WT>;
   using DE = Elem<Promote<XT, WT>::value>;   // dtype of the g*w product
   constexpr int RPB = RowCfg<TPR>::kRowsPerBlock;
@@ -301,22 +303,25 @@ rms_bwd_kernel(const typename Elem<XT>::T* __restrict__ g, const typename Elem<X
 
 // Stage 2 of dw: dw[col] = sum over the partial rows in a fixed order, rounded to w's dtype.
 // A block covers 128 columns (one float4 per lane) with 16 warps; warp i sums partial rows
-// i, i+16, ... with its loads issued 8 at a time, then the 16 warp sums are added in index
-// order.  The order depends only on the partial count, so dw is bitwise reproducible.
+// i, i+16, ... with its loads issued 16 at a time (one L2 round trip for up to 256 partial rows),
+// then the 16 warp sums are added in index order.  The order depends only on the partial count,
+// so dw is bitwise reproducible.
 constexpr int kRedWarps = 16;
+constexpr int kRedBatch = 16;
 template <int WT>
 __global__ void __launch_bounds__(kRedWarps * 32)
 rms_dw_reduce_kernel(const float* __restrict__ part, typename Elem<WT>::T* __restrict__ dw, int nparts, int n) {
+  pdl_enter();
   __shared__ float4 acc[kRedWarps][32];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int col = (blockIdx.x * 32 + lane) * 4;
   const bool vec = (n % 4) == 0;
   float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
   if (col < n) {
-    for (int p0 = wid; p0 < nparts; p0 += 8 * kRedWarps) {
-      float4 v[8];
+    for (int p0 = wid; p0 < nparts; p0 += kRedBatch * kRedWarps) {
+      float4 v[kRedBatch];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u = 0; u < kRedBatch; ++u) {
         const int p = p0 + u * kRedWarps;
         const float* src = part + (int64_t)p * n + col;
         if (p >= nparts) {
@@ -331,7 +336,7 @@ rms_dw_reduce_kernel(const float* __restrict__ part, typename Elem<WT>::T* __res
         }
       }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u = 0; u < kRedBatch; ++u) {
         s.x += v[u].x; s.y += v[u].y; s.z += v[u].z; s.w += v[u].w;
       }
     }
@@ -394,10 +399,9 @@ int run_fwd(const FwdArgs& a) {
   using Cfg = RowCfg<TPR>;
   const int64_t grid = (a.rows + Cfg::kRowsPerBlock - 1) / Cfg::kRowsPerBlock;
   if (grid > 0x7fffffff) return KRSI_ERR_UNSUPPORTED;
-  rms_fwd_kernel<XT, WT, TPR, VEC, NCH><<<(unsigned)grid, Cfg::kThreads, 0, a.s>>>(
-      (const typename Elem<XT>::T*)a.x, (const typename Elem<WT>::T*)a.w, (typename Elem<XT>::T*)a.y, a.rstd,
-      a.rows, a.n, a.eps);
-  KRSI_LAUNCH_CHECK();
+  KRSI_CUDA_TRY(launch_pdl(rms_fwd_kernel<XT, WT, TPR, VEC, NCH>, dim3((unsigned)grid), dim3(Cfg::kThreads), 0, a.s,
+                           (const typename Elem<XT>::T*)a.x, (const typename Elem<WT>::T*)a.w,
+                           (typename Elem<XT>::T*)a.y, a.rstd, a.rows, a.n, a.eps));
   return KRSI_OK;
 }
 
@@ -411,13 +415,12 @@ int run_bwd(const BwdArgs& a) {
   auto kern = rms_bwd_kernel<XT, WT, TPR, VEC, NCH>;
   if (smem > 48 * 1024)
     KRSI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  kern<<<(unsigned)a.nblocks, Cfg::kThreads, smem, a.s>>>(
-      (const typename Elem<XT>::T*)a.g, (const typename Elem<XT>::T*)a.x, (const typename Elem<WT>::T*)a.w,
-      a.rstd, (typename Elem<XT>::T*)a.dx, a.part, a.rows, a.n);
-  KRSI_LAUNCH_CHECK();
-  rms_dw_reduce_kernel<WT><<<(unsigned)((a.n + 127) / 128), kRedWarps * 32, 0, a.s>>>(
-      a.part, (typename Elem<WT>::T*)a.dw, (int)a.nblocks, a.n);
-  KRSI_LAUNCH_CHECK();
+  KRSI_CUDA_TRY(launch_pdl(kern, dim3((unsigned)a.nblocks), dim3(Cfg::kThreads), smem, a.s,
+                           (const typename Elem<XT>::T*)a.g, (const typename Elem<XT>::T*)a.x,
+                           (const typename Elem<WT>::T*)a.w, a.rstd, (typename Elem<XT>::T*)a.dx, a.part, a.rows,
+                           a.n));
+  KRSI_CUDA_TRY(launch_pdl(rms_dw_reduce_kernel<WT>, dim3((unsigned)((a.n + 127) / 128)), dim3(kRedWarps * 32), 0, a.s,
+                           (const float*)a.part, (typename Elem<WT>::T*)a.dw, (int)a.nblocks, a.n));
   return KRSI_OK;
 }
 
