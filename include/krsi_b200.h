@@ -132,6 +132,29 @@ int krsi_relpos_attn_bwd(const void* dout, const void* qkv, int64_t qkv_row_stri
                          int64_t B, int64_t S, int64_t H, int64_t D, float scale,
                          int dtype, cudaStream_t stream);
 
+/* ---------------------------------------------------------------- T5 bucketed relative position
+ * The step either side of the attention op in a T5 model (its relative_attention_bias table).
+ * T5's bucket of a distance rel = key - query (HF transformers T5Attention._relative_position_bucket,
+ * models/t5/modeling_t5.py): with n = num_buckets / 2 if bidirectional (rel > 0 adds n) else
+ * num_buckets, e = n / 2 and a = |rel| (bidirectional) or max(-rel, 0): bucket offset a for a < e,
+ * else e + trunc(log(a / e) / log(max_distance / e) * (n - e)), capped at n - 1.
+ * The reference's attention op takes the bias per distance (pd [H, 2S-1], relpos_attention.py:5);
+ * the reference leaves the table -> pd step and its gradient to torch (an embedding lookup, and
+ * an S x S scatter-add in its backward, LESSONS.md:35). */
+
+/* Bucket of one distance (host-side, no device work): the map the kernels below use. */
+int krsi_t5_bucket(int num_buckets, int max_distance, int bidirectional, int64_t rel, int* bucket);
+
+/* pd[h, t] = table[bucket(t - (S - 1)), h] for t in [0, 2S - 1).
+ * table: [num_buckets, H] of table_dtype (F32, BF16, F16); pd: [H, 2S - 1] fp32. */
+int krsi_t5_bias_fwd(const void* table, float* pd, int64_t S, int64_t H, int num_buckets, int max_distance,
+                     int bidirectional, int table_dtype, cudaStream_t stream);
+
+/* dtable[k, h] = sum of dpd[h, t] over the distances t - (S - 1) in bucket k (a segmented sum in a
+ * fixed order: deterministic), rounded to table_dtype.  dpd: [H, 2S - 1] fp32. */
+int krsi_t5_bias_bwd(const float* dpd, void* dtable, int64_t S, int64_t H, int num_buckets, int max_distance,
+                     int bidirectional, int table_dtype, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

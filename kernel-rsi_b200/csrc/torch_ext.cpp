@@ -175,6 +175,38 @@ std::tuple<at::Tensor, at::Tensor> relpos_attn_bwd(const at::Tensor& dout_in, co
   return {dqkv, dpd};
 }
 
+// ---------------------------------------------------------------- T5 bucketed relative position
+at::Tensor t5_bias_fwd(const at::Tensor& table_in, int64_t S, int64_t num_buckets, int64_t max_distance,
+                       bool bidirectional) {
+  check_cuda(table_in, "table");
+  TORCH_CHECK(table_in.dim() == 2 && table_in.size(0) == num_buckets, "t5_bias: table must be [num_buckets, H]");
+  TORCH_CHECK(S >= 0, "t5_bias: S must be >= 0");
+  c10::cuda::CUDAGuard guard(table_in.device());
+  auto table = table_in.contiguous();
+  auto pd = at::empty({table.size(1), std::max<int64_t>(2 * S - 1, 0)}, table.options().dtype(at::kFloat));
+  check_rc(krsi_t5_bias_fwd(table.data_ptr(), pd.data_ptr<float>(), S, table.size(1), (int)num_buckets,
+                            (int)max_distance, bidirectional ? 1 : 0, krsi_dtype_of(table),
+                            at::cuda::getCurrentCUDAStream()),
+           "krsi_t5_bias_fwd");
+  return pd;
+}
+
+at::Tensor t5_bias_bwd(const at::Tensor& dpd_in, const at::Tensor& table, int64_t S, int64_t num_buckets,
+                       int64_t max_distance, bool bidirectional) {
+  check_cuda(dpd_in, "dpd");
+  TORCH_CHECK(table.dim() == 2 && table.size(0) == num_buckets, "t5_bias_bwd: table must be [num_buckets, H]");
+  TORCH_CHECK(dpd_in.dim() == 2 && dpd_in.size(0) == table.size(1) && dpd_in.size(1) == std::max<int64_t>(2 * S - 1, 0),
+              "t5_bias_bwd: dpd must be [H, 2S-1]");
+  c10::cuda::CUDAGuard guard(dpd_in.device());
+  auto dpd = dpd_in.to(at::kFloat).contiguous();
+  auto dtable = at::empty(table.sizes(), table.options().memory_format(at::MemoryFormat::Contiguous));
+  check_rc(krsi_t5_bias_bwd(dpd.data_ptr<float>(), dtable.data_ptr(), S, table.size(1), (int)num_buckets,
+                            (int)max_distance, bidirectional ? 1 : 0, krsi_dtype_of(table),
+                            at::cuda::getCurrentCUDAStream()),
+           "krsi_t5_bias_bwd");
+  return dtable;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(krsi, m) {
@@ -185,6 +217,8 @@ TORCH_LIBRARY(krsi, m) {
   m.def("relpos_attn_fwd(Tensor qkv, Tensor pd, int B, int S, int H, int D, float scale) -> (Tensor, Tensor, Tensor)");
   m.def("relpos_attn_bwd(Tensor dout, Tensor qkv, Tensor pd, Tensor out32, Tensor lse, int B, int S, int H, int D, "
         "float scale) -> (Tensor, Tensor)");
+  m.def("t5_bias_fwd(Tensor table, int S, int num_buckets, int max_distance, bool bidirectional) -> Tensor");
+  m.def("t5_bias_bwd(Tensor dpd, Tensor table, int S, int num_buckets, int max_distance, bool bidirectional) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(krsi, CUDA, m) {
@@ -194,4 +228,6 @@ TORCH_LIBRARY_IMPL(krsi, CUDA, m) {
   m.impl("geglu_bwd", &geglu_bwd);
   m.impl("relpos_attn_fwd", &relpos_attn_fwd);
   m.impl("relpos_attn_bwd", &relpos_attn_bwd);
+  m.impl("t5_bias_fwd", &t5_bias_fwd);
+  m.impl("t5_bias_bwd", &t5_bias_bwd);
 }

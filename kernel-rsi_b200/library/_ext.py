@@ -101,6 +101,14 @@ def _register_compile_support() -> None:
     def _(dout, qkv, pd, out32, lse, B, S, H, D, scale):
         return qkv.new_empty((B * S, 3 * H * D)), pd.new_empty((H, max(2 * S - 1, 0)), dtype=torch.float32)
 
+    @reg_fake("krsi::t5_bias_fwd")
+    def _(table, S, num_buckets, max_distance, bidirectional):
+        return table.new_empty((table.shape[1], max(2 * S - 1, 0)), dtype=torch.float32)
+
+    @reg_fake("krsi::t5_bias_bwd")
+    def _(dpd, table, S, num_buckets, max_distance, bidirectional):
+        return torch.empty_like(table)
+
     # Autograd of the forward ops, used when a compiled graph contains them (the eager path
     # uses the autograd.Function classes of each module instead).
     def rms_setup(ctx, inputs, output):
@@ -132,6 +140,17 @@ def _register_compile_support() -> None:
         return dqkv, dpd, None, None, None, None, None
 
     torch.library.register_autograd("krsi::relpos_attn_fwd", attn_backward, setup_context=attn_setup)
+
+    def t5_setup(ctx, inputs, output):
+        table, S, nb, md, bi = inputs
+        ctx.save_for_backward(table)
+        ctx.args = (S, nb, md, bi)
+
+    def t5_backward(ctx, dpd):
+        (table,) = ctx.saved_tensors
+        return ops.t5_bias_bwd(dpd.contiguous(), table, *ctx.args), None, None, None, None
+
+    torch.library.register_autograd("krsi::t5_bias_fwd", t5_backward, setup_context=t5_setup)
 
 
 _register_compile_support()
