@@ -1,0 +1,151 @@
+"""The drop-in on a whole model, the way the reference's tools check it: a T5 v1.1 encoder stack
+(kernel-rsi_b200/t5_block/model_entry.py, the tools' model-entry contract) with its T5Block.forward
+replaced by impl.py (the library ops), installed the way swap.py and the exported krsi_patch.apply()
+install it (a bound `forward` on each module instance: tools/swap.py:67-76, tools/report.py:86-106).
+
+- Always (GPU): the check swap.py makes (tools/swap.py:87-152): loss, output and every parameter
+  gradient of the patched bf16 model against the original run in fp32 (TF32 off), under the
+  reference's compare() criterion with slack 2 against the bf16 original, on build() and shapes()
+  inputs; and apply()/remove() of a krsi_patch-style export.
+- With KRSI_REFERENCE pointing at a kernel-rsi checkout on a GPU host: the unchanged tools themselves
+  (region.py -> bench.py -> swap.py -> report.py, and replay.py over this library) on a skill tree
+  assembled from the checkout's tools/ and this repository's library/.  The reference is not present
+  on a machine without that checkout (and its sources are not copied into this repository), so there
+  those two tests skip and say why."""
+import copy
+import importlib.util
+import os
+import shutil
+import subprocess
+import sys
+import types
+from pathlib import Path
+
+import pytest
+import torch
+
+from conftest import PKG, ROOT
+from oracle.compare import compare, norm_max_err
+
+pytestmark = pytest.mark.gpu
+T5_DIR = PKG / "t5_block"
+
+
+def load(path, name):
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+@pytest.fixture(scope="module")
+def entry():
+    return load(T5_DIR / "model_entry.py", "krsi_t5_model_entry")
+
+
+@pytest.fixture(scope="module")
+def impl():
+    return load(T5_DIR / "impl.py", "krsi_t5_impl")
+
+
+def install(model, impl, cls):
+    for m in model.modules():
+        if isinstance(m, cls):
+            m.forward = types.MethodType(lambda self, *x, _i=impl, **k: _i.forward(self, *x, **k), m)
+
+
+def step(entry, model, x):
+    out = model(*x)
+    loss = entry.loss(out, x)
+    ps = [p for p in model.parameters() if p.requires_grad]
+    grads = torch.autograd.grad(loss, ps)
+    return [loss.detach().reshape(1), out.detach()] + [g.detach() for g in grads]
+
+
+def test_swap_check_on_the_whole_model(entry, impl):
+    model, inputs = entry.build()
+    model.train()
+    for x in [inputs] + list(entry.shapes()):
+        ref_model = copy.deepcopy(model).float()
+        prev = torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = torch.backends.cudnn.allow_tf32 = False
+        try:
+            ref32 = step(entry, ref_model, tuple(t.float() for t in x))
+        finally:
+            torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = prev
+        orig = step(entry, model, x)
+        patched = copy.deepcopy(model)
+        install(patched, impl, entry.T5Block)
+        cand = step(entry, patched, x)
+        res = compare([r.float() for r in ref32], [o.float() for o in orig], [c.float() for c in cand])
+        names = ["loss", "out"] + [n for n, _ in model.named_parameters()]
+        assert res["pass"], [(n, o) for n, o in zip(names, res["outputs"]) if not o.get("passed", True)]
+        for n, c, r in zip(names, cand, ref32):
+            assert norm_max_err(c.float(), r.float()) <= 1e-2, n
+
+
+def test_krsi_patch_apply_and_remove(entry, impl):
+    """What report.py exports (krsi_patch.apply/remove): bound forwards on the module instances."""
+    model, (x,) = entry.build()
+    base = model(x)
+    blocks = [m for m in model.modules() if isinstance(m, entry.T5Block)]
+    for m in blocks:   # apply(model)
+        m.forward = types.MethodType(lambda self, *a, _i=impl, **k: _i.forward(self, *a, **k), m)
+    patched = model(x)
+    assert norm_max_err(patched.float(), base.float()) <= 1e-2
+    for m in blocks:   # remove(model)
+        m.__dict__.pop("forward", None)
+    assert torch.equal(model(x), base)
+
+
+def reference_checkout():
+    ref = os.environ.get("KRSI_REFERENCE")
+    if not ref or not (Path(ref) / "tools" / "swap.py").is_file():
+        pytest.skip("KRSI_REFERENCE does not point at a kernel-rsi checkout with tools/ "
+                    "(the reference is not on this machine and is not copied into this repository)")
+    return Path(ref)
+
+
+def skill_tree(tmp_path, ref):
+    """tools/ from the checkout, library/ = this repository's library (a copy, so that the tools'
+    outputs under library/replay stay out of the repository)."""
+    skill = tmp_path / "skill"
+    skill.mkdir()
+    (skill / "tools").symlink_to(ref / "tools")
+    shutil.copytree(PKG / "library", skill / "library", ignore=shutil.ignore_patterns("__pycache__"))
+    (skill / "lib").symlink_to(PKG / "lib")          # _ext.py finds the native libraries at ../lib
+    return skill
+
+
+def run_tool(skill, *args, cwd):
+    env = dict(os.environ, PYTHONPATH=str(PKG / "library"))
+    p = subprocess.run([sys.executable, str(skill / "tools" / args[0]), *args[1:]], cwd=cwd, env=env,
+                       text=True, capture_output=True, timeout=1800)
+    return p.returncode, p.stdout + p.stderr
+
+
+def test_reference_replay_over_this_library(tmp_path):
+    ref = reference_checkout()
+    skill = skill_tree(tmp_path, ref)
+    rc, out = run_tool(skill, "replay.py", cwd=tmp_path)
+    assert rc == 0, out[-3000:]
+    for op in ("rmsnorm", "geglu", "relpos_attention", "t5_bias"):
+        assert f"{op}" in out and "FAIL" not in out.split(op, 1)[1].splitlines()[0], out[-3000:]
+
+
+def test_reference_tools_flow_on_the_t5_block(tmp_path):
+    ref = reference_checkout()
+    skill = skill_tree(tmp_path, ref)
+    work = tmp_path / "work"
+    entry_py = T5_DIR / "model_entry.py"
+    rc, out = run_tool(skill, "region.py", "--entry", str(entry_py), "--module", "layers.0", "--out",
+                       str(work / "r0"), cwd=tmp_path)
+    assert rc == 0, out[-3000:]
+    shutil.copy(T5_DIR / "impl.py", work / "r0" / "impl.py")
+    rc, out = run_tool(skill, "bench.py", str(work / "r0"), cwd=tmp_path)
+    assert rc == 0, out[-3000:]
+    rc, out = run_tool(skill, "swap.py", "--entry", str(entry_py), "--impl", str(work / "r0"), "--all-instances",
+                       cwd=tmp_path)
+    assert rc == 0, out[-3000:]
+    rc, out = run_tool(skill, "report.py", str(work), cwd=tmp_path)
+    assert rc == 0 and (work / "krsi_patch.py").is_file(), out[-3000:]
