@@ -34,56 +34,18 @@ __device__ __forceinline__ GeluParts gelu_parts(float a) {
   return {t, 0.5f * a * (1.0f + t)};
 }
 
-// The float -> 16-bit conversions run on the same pipe (XU) as ex2 and the reciprocal, and with
-// one conversion per rounding point they, not HBM, bounded these kernels (about 4.4 XU
-// instructions per element in the forward).  So: a rounding point that stays in fp32 (x rounded to
-// bf16 and read back) is done with integer ops on the ALU pipe, and results are stored through
-// packed two-element conversions.  Both round to nearest, ties to even, exactly as cvt.rn does.
-__device__ __forceinline__ float round_bf16_alu(float x) {
-  const uint32_t u = __float_as_uint(x);
-  const uint32_t r = (u + 0x7fffu + ((u >> 16) & 1u)) & 0xffff0000u;
-  return __uint_as_float((u & 0x7fffffffu) > 0x7f800000u ? (u | 0x00400000u) & 0xffff0000u : r);   // NaN stays NaN
-}
-template <int DT>
-__device__ __forceinline__ float rnd(float x) {
-  if constexpr (DT == KRSI_BF16) return round_bf16_alu(x);
-  else return Elem<DT>::round(x);
-}
-// Two floats -> one 32-bit word of two 16-bit values (lo in the low half).
-template <int DT>
-__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-  uint32_t d;
-  if constexpr (DT == KRSI_BF16) asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
-  else asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
-  return d;
-}
-// Stores VEC floats as one 16-byte packet of the element type.
-template <int DT, int VEC>
-__device__ __forceinline__ void store_packet(typename Elem<DT>::T* dst, const float* v) {
-  using T = typename Elem<DT>::T;
-  if constexpr (DT == KRSI_F32) {
-    *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
-  } else {
-    uint32_t w[VEC / 2];
-#pragma unroll
-    for (int e = 0; e < VEC; e += 2) w[e / 2] = pack2<DT>(v[e], v[e + 1]);
-    *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
-  }
-  (void)sizeof(T);
-}
-
-// out before its final rounding (the store rounds it): gel rounded to the dtype, times b.
 template <int DT>
 __device__ __forceinline__ float geglu_out(float a, float b) {
-  return rnd<DT>(gelu_parts(a).gel) * b;
+  using E = Elem<DT>;
+  return E::round(E::round(gelu_parts(a).gel) * b);
 }
 
-// da and db before their final rounding (the store rounds them).
 template <int DT>
 __device__ __forceinline__ void geglu_grad(float a, float b, float g, float* da, float* db) {
+  using E = Elem<DT>;
   const GeluParts p = gelu_parts(a);
-  *db = g * rnd<DT>(p.gel);
-  const float dgel = rnd<DT>(g * b);
+  *db = E::round(g * E::round(p.gel));
+  const float dgel = E::round(g * b);
   const float dz = kSqrt2OverPi * (1.0f + 3.0f * kGeluC * a * a);
   *da = dgel * (0.5f * (1.0f + p.t) + 0.5f * a * (1.0f - p.t * p.t) * dz);
 }
@@ -109,14 +71,14 @@ geglu_fwd_vec(const typename Elem<DT>::T* __restrict__ u, typename Elem<DT>::T* 
     const auto a0 = ldg16_stream(u0), b0 = ldg16_stream(u0 + (size_t)FV * VEC);
     Vec16<T> a1, b1;
     if (has1) { a1 = ldg16_stream(u1); b1 = ldg16_stream(u1 + (size_t)FV * VEC); }
-    float o[VEC];
+    Vec16<T> o0, o1;
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) o[e] = geglu_out<DT>(E::load(a0.v[e]), E::load(b0.v[e]));
-    store_packet<DT, VEC>(out + (size_t)i0 * VEC, o);
+    for (int e = 0; e < VEC; ++e) o0.v[e] = E::store(geglu_out<DT>(E::load(a0.v[e]), E::load(b0.v[e])));
+    stg16(out + (size_t)i0 * VEC, o0);
     if (has1) {
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) o[e] = geglu_out<DT>(E::load(a1.v[e]), E::load(b1.v[e]));
-      store_packet<DT, VEC>(out + (size_t)i1 * VEC, o);
+      for (int e = 0; e < VEC; ++e) o1.v[e] = E::store(geglu_out<DT>(E::load(a1.v[e]), E::load(b1.v[e])));
+      stg16(out + (size_t)i1 * VEC, o1);
     }
   }
 }
@@ -136,11 +98,16 @@ geglu_bwd_vec(const typename Elem<DT>::T* __restrict__ g, const typename Elem<DT
     const auto av = ldg16_stream(u + ua);
     const auto bv = ldg16_stream(u + ua + (size_t)FV * VEC);
     const auto gv = ldg16_stream(g + (size_t)i * VEC);
-    float dav[VEC], dbv[VEC];
+    Vec16<T> dav, dbv;
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) geglu_grad<DT>(E::load(av.v[e]), E::load(bv.v[e]), E::load(gv.v[e]), &dav[e], &dbv[e]);
-    store_packet<DT, VEC>(du + ua, dav);
-    store_packet<DT, VEC>(du + ua + (size_t)FV * VEC, dbv);
+    for (int e = 0; e < VEC; ++e) {
+      float da, db;
+      geglu_grad<DT>(E::load(av.v[e]), E::load(bv.v[e]), E::load(gv.v[e]), &da, &db);
+      dav.v[e] = E::store(da);
+      dbv.v[e] = E::store(db);
+    }
+    stg16(du + ua, dav);
+    stg16(du + ua + (size_t)FV * VEC, dbv);
   }
 }
 
@@ -155,7 +122,7 @@ geglu_fwd_scalar(const typename Elem<DT>::T* __restrict__ u, typename Elem<DT>::
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / F, c = i - r * F;
     const float a = E::load(u[r * 2 * F + c]), b = E::load(u[r * 2 * F + F + c]);
-    out[i] = E::store(geglu_out<DT>(a, b));   // the store is the final rounding point
+    out[i] = E::store(geglu_out<DT>(a, b));
   }
 }
 

@@ -84,8 +84,22 @@ t5_bias_fwd_kernel(const typename Elem<DT>::T* __restrict__ table, float* __rest
   }
 }
 
-// One warp per (bucket, head): lanes take the bucket's run of t in strides of 32, in order, then
-// a fixed butterfly adds the lanes.
+// Distances a (>= 0) of bucket offset k on one side: [lo, hi), hi = INT64_MAX for the last offset.
+__device__ __forceinline__ void offset_range(const BucketMap& m, int k, int64_t* lo, int64_t* hi) {
+  const int64_t kInf = 0x7fffffffffffffffLL;
+  if (k < m.exact) {
+    *lo = k;
+    *hi = k + 1;
+  } else {
+    const int j = k - m.exact;                  // 0 .. n_thr
+    *lo = j == 0 ? m.exact : m.thr[j - 1];
+    *hi = j < m.n_thr ? m.thr[j] : kInf;
+  }
+}
+
+// One warp per (bucket, head).  A bucket is one run of distances on each side of rel = 0, found in
+// closed form from the thresholds; the lanes add the run's dpd in strides of 32, in order, then a
+// fixed butterfly adds the lanes (deterministic).
 template <int DT>
 __global__ void __launch_bounds__(256)
 t5_bias_bwd_kernel(const float* __restrict__ dpd, typename Elem<DT>::T* __restrict__ dtable, int64_t S, int H,
@@ -95,27 +109,25 @@ t5_bias_bwd_kernel(const float* __restrict__ dpd, typename Elem<DT>::T* __restri
   if (warp >= num_buckets * H) return;
   const int k = warp / H, h = warp % H;
   const int64_t n = 2 * S - 1;
-  // the run of t whose bucket is k: bucket_of is monotone on each side, so scan for its ends
-  // with a binary search per side of rel = 0
-  auto lower = [&](int64_t lo, int64_t hi, int target, bool increasing) {   // first t in [lo, hi) reaching target
-    while (lo < hi) {
-      const int64_t mid = lo + (hi - lo) / 2;
-      const int b = bucket_of(m, mid - (S - 1));
-      if (increasing ? (b >= target) : (b <= target)) hi = mid;
-      else lo = mid + 1;
-    }
-    return lo;
-  };
   const float* row = dpd + (int64_t)h * n;
   float s = 0.f;
-  // rel <= 0 (t in [0, S)): bucket non-increasing in t; rel > 0 (t in [S, n)): non-decreasing
-  {
-    const int64_t a = lower(0, S, k, false), b = lower(0, S, k - 1, false);
-    for (int64_t t = a + lane; t < b; t += 32) s += row[t];
-  }
-  {
-    const int64_t a = lower(S, n, k, true), b = lower(S, n, k + 1, true);
-    for (int64_t t = a + lane; t < b; t += 32) s += row[t];
+  auto add_run = [&](int64_t t0, int64_t t1) {   // t in [t0, t1)
+    for (int64_t t = t0 + lane; t < t1; t += 32) s += row[t];
+  };
+  int64_t lo, hi;
+  if (m.bidir) {
+    if (k < m.n_side) {                         // rel = -a <= 0: t = S - 1 - a
+      offset_range(m, k, &lo, &hi);
+      if (lo <= S - 1) add_run(S - 1 - min(hi - 1, S - 1), S - lo);
+    } else {                                    // rel = a > 0: t = S - 1 + a
+      offset_range(m, k - m.n_side, &lo, &hi);
+      lo = max(lo, (int64_t)1);
+      if (lo <= S - 1) add_run(S - 1 + lo, S - 1 + min(hi - 1, S - 1) + 1);
+    }
+  } else {
+    offset_range(m, k, &lo, &hi);               // rel = -a <= 0
+    if (lo <= S - 1) add_run(S - 1 - min(hi - 1, S - 1), S - lo);
+    if (k == 0) add_run(S, n);                  // every rel > 0 is bucket 0
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);

@@ -80,22 +80,30 @@ def test_swap_check_on_the_whole_model(entry, impl):
         res = compare([r.float() for r in ref32], [o.float() for o in orig], [c.float() for c in cand])
         names = ["loss", "out"] + [n for n, _ in model.named_parameters()]
         assert res["pass"], [(n, o) for n, o in zip(names, res["outputs"]) if not o.get("passed", True)]
-        for n, c, r in zip(names, cand, ref32):
-            assert norm_max_err(c.float(), r.float()) <= 1e-2, n
+        # and each tensor's normalised max error within 1e-2, or within the bf16 original's own
+        # error where that is larger (RMSNorm weight gradients of this model: about 1e-2)
+        for n, c, o, r in zip(names, cand, orig, ref32):
+            e_c, e_o = norm_max_err(c.float(), r.float()), norm_max_err(o.float(), r.float())
+            assert e_c <= max(1e-2, e_o), (n, e_c, e_o)
 
 
 def test_krsi_patch_apply_and_remove(entry, impl):
     """What report.py exports (krsi_patch.apply/remove): bound forwards on the module instances."""
     model, (x,) = entry.build()
-    base = model(x)
-    blocks = [m for m in model.modules() if isinstance(m, entry.T5Block)]
-    for m in blocks:   # apply(model)
-        m.forward = types.MethodType(lambda self, *a, _i=impl, **k: _i.forward(self, *a, **k), m)
-    patched = model(x)
-    assert norm_max_err(patched.float(), base.float()) <= 1e-2
-    for m in blocks:   # remove(model)
-        m.__dict__.pop("forward", None)
-    assert torch.equal(model(x), base)
+    with torch.no_grad():
+        base = model(x)
+        h = x
+        for layer in model.layers:                   # the replacement, called directly
+            h = impl.forward(layer, h)
+        blocks = [m for m in model.modules() if isinstance(m, entry.T5Block)]
+        assert len(blocks) == len(model.layers)
+        for m in blocks:   # apply(model)
+            m.forward = types.MethodType(lambda self, *a, _i=impl, **k: _i.forward(self, *a, **k), m)
+        patched = model(x)
+        assert torch.equal(patched, h)               # every block now runs the library ops
+        for m in blocks:   # remove(model)
+            m.__dict__.pop("forward", None)
+        assert torch.equal(model(x), base)           # and the original forward is back
 
 
 def reference_checkout():
