@@ -500,8 +500,10 @@ class BlockWorkload:
     kernel_key = "relpos_attention fwd+bwd (in block step)"
     # our kernels per layer per step: rmsnorm 2 x (fwd 1 + bwd 2), attention fwd 1 + bwd 5, geglu 2
     LAUNCHES_PER_LAYER = 14
-    # gradient all-reduce bucket: the bf16 weights of this many layers (tunable: KRSI_BUCKET_LAYERS)
-    LAYERS_PER_BUCKET = int(os.environ.get("KRSI_BUCKET_LAYERS", "1"))
+    # gradient all-reduce buckets: the bf16 weights of this many layers, the last TAIL layers one each
+    # (tunable: KRSI_BUCKET_LAYERS, KRSI_BUCKET_TAIL)
+    LAYERS_PER_BUCKET = int(os.environ.get("KRSI_BUCKET_LAYERS", "4"))
+    TAIL_LAYERS = int(os.environ.get("KRSI_BUCKET_TAIL", "2"))
 
     def __init__(self, rank, world):
         import harness.block as hb
@@ -517,7 +519,7 @@ class BlockWorkload:
         return {"workload": "block stack (config 5) fwd+bwd", "layers": c.layers, "global_batch": self.GLOBAL_B,
                 "seq_len": c.seq, "d_model": c.d, "heads": c.heads, "head_dim": c.head_dim, "ffn": c.ffn,
                 "parallelism": f"dp{self.world} (batch-sharded, NCCL grad all-reduce)",
-                "allreduce_bucket_layers": self.LAYERS_PER_BUCKET,
+                "allreduce_bucket_layers": self.LAYERS_PER_BUCKET, "allreduce_tail_layers": self.TAIL_LAYERS,
                 "flop_per_step": self.work, "l2": "inputs and activations >> L2",
                 "timing": "one CUDA graph replay per step (forward, backward, bucketed all-reduce), CUDA events"}
 
@@ -533,7 +535,8 @@ class BlockWorkload:
         self.setup_host()
         self.model = hb.BlockStack(self.cfg, hb.LibraryOps(), dev, seed=0)
         self.timer = hb.AttentionTimer(self.model)
-        self.reducer = LayerBucketAllReduce(self.model.layers, layers_per_bucket=self.LAYERS_PER_BUCKET)
+        self.reducer = LayerBucketAllReduce(self.model.layers, layers_per_bucket=self.LAYERS_PER_BUCKET,
+                                            tail_layers=self.TAIL_LAYERS)
         x = shard_batch(self.x_global, self.rank, self.world)
         self.x = x.to(dev)
         self.x_pinned = x.contiguous().pin_memory()

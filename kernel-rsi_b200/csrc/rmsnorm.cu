@@ -25,6 +25,13 @@ template <int TPR> struct RowCfg {
   static constexpr int kThreads = TPR == 32 ? 256 : TPR;   // block size
   static constexpr int kRowsPerBlock = kThreads / TPR;      // rows processed together
 };
+// The forward's warp-per-row blocks hold two rows: its blocks are independent, so small blocks
+// spread a few thousand rows evenly over the SMs (2048 rows: 1024 blocks, 6.9 per SM, instead of
+// 256 blocks of which some SMs run two and others one).
+template <int TPR> struct FwdRowCfg {
+  static constexpr int kThreads = TPR == 32 ? 64 : TPR;
+  static constexpr int kRowsPerBlock = kThreads / TPR;
+};
 
 // Sum over the TPR threads that share a row (a warp, or the whole block).
 template <int TPR>
@@ -66,14 +73,14 @@ __device__ __forceinline__ void store_vec(typename Elem<DT>::T* p, const float* 
 }
 
 template <int XT, int WT, int TPR, int VEC, int NCH>
-__global__ void __launch_bounds__(RowCfg<TPR>::kThreads)
+__global__ void __launch_bounds__(FwdRowCfg<TPR>::kThreads)
 rms_fwd_kernel(const typename Elem<XT>::T* __restrict__ x, const typename Elem<WT>::T* __restrict__ w,
                typename Elem<XT>::T* __restrict__ y, float* __restrict__ rstd, int64_t rows, int n, float eps) {
   pdl_enter();
   using WE = Elem<WT>;
   __shared__ float red[32];
   const int t = threadIdx.x % TPR;
-  const int64_t row = (int64_t)blockIdx.x * RowCfg<TPR>::kRowsPerBlock + threadIdx.x / TPR;
+  const int64_t row = (int64_t)blockIdx.x * FwdRowCfg<TPR>::kRowsPerBlock + threadIdx.x / TPR;
   const bool live = row < rows;   // a block-per-row group is always live
   const auto* xr = x + row * n;
   float xv[NCH][VEC];
@@ -396,7 +403,7 @@ struct BwdArgs {
 
 template <int XT, int WT, int TPR, int VEC, int NCH>
 int run_fwd(const FwdArgs& a) {
-  using Cfg = RowCfg<TPR>;
+  using Cfg = FwdRowCfg<TPR>;
   const int64_t grid = (a.rows + Cfg::kRowsPerBlock - 1) / Cfg::kRowsPerBlock;
   if (grid > 0x7fffffff) return KRSI_ERR_UNSUPPORTED;
   KRSI_CUDA_TRY(launch_pdl(rms_fwd_kernel<XT, WT, TPR, VEC, NCH>, dim3((unsigned)grid), dim3(Cfg::kThreads), 0, a.s,

@@ -7,9 +7,11 @@ packing copies are needed, and a bucket is launched asynchronously (NCCL's own s
 autograd has accumulated its last gradient, so its communication overlaps the rest of the backward.
 
 Buckets: the bf16 weights of `layers_per_bucket` consecutive layers (backward order: the last
-layers' bucket fills first), and the small fp32 tensors of every layer (the relative-position
-tables, 131 KB a layer) in one bucket of their own, launched when the first layer's table gradient
-lands near the end of the backward (one collective instead of one latency-bound call per layer).
+layers' bucket fills first), except the first `tail_layers` layers, which get one bucket each (the
+final buckets' all-reduces cannot overlap any backward work, so they are kept small), and the small
+fp32 tensors of every layer (the relative-position tables, 131 KB a layer) in one bucket of their
+own, launched when the first layer's table gradient lands near the end of the backward (one
+collective instead of one latency-bound call per layer).
 """
 from __future__ import annotations
 
@@ -20,7 +22,8 @@ import torch.distributed as dist
 
 
 class LayerBucketAllReduce:
-    def __init__(self, layers, group=None, layers_per_bucket: int = 1, small_bytes: int = 1 << 20):
+    def __init__(self, layers, group=None, layers_per_bucket: int = 1, small_bytes: int = 1 << 20,
+                 tail_layers: int = 0):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.buckets = []       # (bucket key, dtype, flat buffer, [params])
@@ -47,6 +50,8 @@ class LayerBucketAllReduce:
                     continue
                 if per_layer_bytes[p.dtype] < small_bytes:
                     key = ("all", p.dtype)                              # one bucket for all layers
+                elif li < tail_layers:
+                    key = (("tail", li), p.dtype)                       # the last layers: one bucket each
                 else:
                     key = ((n - 1 - li) // max(1, layers_per_bucket), p.dtype)
                 groups[key].append(p)

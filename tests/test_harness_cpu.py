@@ -76,7 +76,8 @@ def _worker(rank, world, port, q, mode):
         model = make_model(cfg)
         # "ok": default buckets (this tiny model's tensors all fall in the one small-tensor bucket);
         # "per_layer": one bucket per layer and dtype; "pairs": two layers per bucket
-        kw = {"per_layer": dict(small_bytes=0), "pairs": dict(small_bytes=0, layers_per_bucket=2)}.get(mode, {})
+        kw = {"per_layer": dict(small_bytes=0), "pairs": dict(small_bytes=0, layers_per_bucket=2),
+              "tail": dict(small_bytes=0, layers_per_bucket=2, tail_layers=1)}.get(mode, {})
         reducer = LayerBucketAllReduce(model.layers, **kw)
         if mode == "die" and rank == 1:
             raise RuntimeError("planted failure on rank 1 before its first collective")
@@ -111,7 +112,7 @@ def run_ranks(world, mode):
     return out
 
 
-@pytest.mark.parametrize("mode", ["ok", "per_layer", "pairs"])
+@pytest.mark.parametrize("mode", ["ok", "per_layer", "pairs", "tail"])
 def test_two_rank_gradients_equal_full_batch(mode):
     from harness.block import loss_fn
     from harness.grad_sync import LayerBucketAllReduce, train_step
@@ -139,6 +140,11 @@ def test_bucket_plan():
     # bf16 weights: layers (3, 2) and (1, 0) in backward order; the fp32 tables of all layers: one bucket
     assert sorted(k for k in keys if k[1] == torch.bfloat16) == [(0, torch.bfloat16), (1, torch.bfloat16)]
     assert (("all", torch.float32)) in keys and len(keys) == 3
+    red.remove()
+    red = LayerBucketAllReduce(model.layers, layers_per_bucket=2, small_bytes=1024, tail_layers=2)
+    keys = [k[0] for k, _, _, _ in red.buckets if k[1] == torch.bfloat16]
+    # layers 3 and 2 share a bucket; layers 1 and 0 (the last two of the backward) get one each
+    assert sorted(map(str, keys)) == sorted(map(str, [0, ("tail", 1), ("tail", 0)]))
     for _, _, flat, params in red.buckets:
         assert sum(p.numel() for p in params) == flat.numel()
         assert all(p.grad.data_ptr() >= flat.data_ptr() for p in params)
