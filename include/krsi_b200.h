@@ -71,6 +71,15 @@ int krsi_rmsnorm_bwd(const void* g, const void* x, const void* w, const float* r
                      void* dx, void* dw, void* workspace, size_t workspace_bytes,
                      int64_t rows, int64_t n, int x_dtype, int w_dtype, cudaStream_t stream);
 
+/* The same backward with a second gradient of x added: dx = (the backward above) + gadd, rounded
+ * once.  For a pre-norm residual block, where x also feeds the residual branch and autograd would
+ * otherwise add the two gradients of x in a separate pass (read both, write the sum).  No
+ * counterpart in the reference (its backward returns dx alone, rmsnorm.py:62-68).
+ * gadd: [rows, n] of x_dtype (16-byte aligned when n is a multiple of the vector width). */
+int krsi_rmsnorm_bwd_add(const void* g, const void* x, const void* w, const float* rstd, const void* gadd,
+                         void* dx, void* dw, void* workspace, size_t workspace_bytes,
+                         int64_t rows, int64_t n, int x_dtype, int w_dtype, cudaStream_t stream);
+
 /* The same backward for callers that cannot allocate device memory (a host that owns all device
  * memory, or a loop that must not stall on cudaMalloc): the dw partial sums live in a fixed
  * device array inside this library (4 MiB per GPU that loads it, kept until the process exits)

@@ -128,6 +128,44 @@ __device__ __forceinline__ void fill_row_rev(float* dst, int n, int top, const f
   }
 }
 
+// The two copies fill_row_rev(dst0, n, top, ...) and fill_row_rev(dst1, n, top - 1, ...) in one
+// pass over the source (dst1[i] = dst0[i + 1]): one global round trip instead of two.
+__device__ __forceinline__ void fill_row_rev2(float* dst0, float* dst1, int n, int top, const float* __restrict__ src,
+                                              int lo, int hi, float mul, int tid, int nthr) {
+  const int len = hi >= lo ? hi - lo + 1 : 0;
+  const int mis = (int)((reinterpret_cast<uintptr_t>(src + lo) >> 2) & 3);
+  const int a0 = lo + (mis ? min(4 - mis, len) : 0);   // first aligned source index
+  const int nvec = lo + len > a0 ? (lo + len - a0) / 4 : 0;
+  const int a1 = a0 + 4 * nvec;
+  const float4* src4 = reinterpret_cast<const float4*>(src + a0);
+  auto put = [&](int i, float v) {            // source element whose dst0 index is i
+    if (i >= 0 && i < n) dst0[i] = v;
+    if (i >= 1 && i - 1 < n) dst1[i - 1] = v;
+  };
+  for (int v0 = tid; v0 < nvec; v0 += 4 * nthr) {
+    float4 x[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (v0 + u * nthr < nvec) x[u] = __ldg(src4 + v0 + u * nthr);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = top - (a0 + 4 * (v0 + u * nthr));
+      if (v0 + u * nthr < nvec) {
+        put(i, x[u].x * mul);
+        put(i - 1, x[u].y * mul);
+        put(i - 2, x[u].z * mul);
+        put(i - 3, x[u].w * mul);
+      }
+    }
+  }
+  for (int i = tid; i < n; i += nthr) {
+    const int m0 = top - i, m1 = top - 1 - i;
+    if (m0 < lo || m0 > hi) dst0[i] = 0.f;
+    else if (m0 < a0 || m0 >= a1) dst0[i] = __ldg(src + m0) * mul;
+    if (m1 < lo || m1 > hi) dst1[i] = 0.f;
+    else if (m1 < a0 || m1 >= a1) dst1[i] = __ldg(src + m1) * mul;
+  }
+}
 // ---------------------------------------------------------------- host side
 using EncodeTiledFn = PFN_cuTensorMapEncodeTiled_v12000;
 

@@ -23,8 +23,9 @@
 //                              S^T = K Q^T, dP^T = V dO^T              (SS, K = DP)
 //                              dV += P^T dO, dK += dS^T Q               (TS: P^T/dS^T in TMEM)
 //                              dQ  = dS K                              (SS: dS staged in smem)
-//                warps 2-15  first fill the resident bias rows: a reversed window of the bias
-//                            row, in two copies (the second shifted by one, for aligned pairs)
+//                warps 2, 4-15 first fill the resident bias rows: a reversed window of the bias
+//                            row, in two copies (the second shifted by one, for aligned pairs),
+//                            while warp 3 publishes the first stage
 //                warps 4-11  two compute warpgroups, one key row per thread and 64 queries per
 //                            warpgroup: P^T, dS^T in paired fp32 -> 16-bit into TMEM and smem;
 //                            dBias diagonal sums of the fp32 dS by a warp-shuffle transpose into
@@ -65,7 +66,10 @@ constexpr uint32_t kRegsCompute = 160;
 constexpr uint32_t kRegsDq = 88;
 constexpr int kWarpsPerTile = 8;    // dBias partial rows per tile: (query half, key quarter)
 constexpr int kBins = 96;           // per-warp bins: 32 keys x 64 queries -> 95 diagonals (+1 zero)
-constexpr int kRowFillers = 448;    // warps 2-15 fill the resident rows (compute warps: before their first P)
+// warps 2 and 4-15 fill the resident rows (compute warps: before their first P); warp 3 publishes
+// the first Q/dO stage meanwhile, so the first S^T and dP^T are computed while the rows load
+constexpr int kRowFillers = 416;
+__device__ __forceinline__ int filler_id() { return (int)threadIdx.x - (threadIdx.x < 96 ? 64 : 96); }
 constexpr int kCopyBank = 16;       // distance (mod 32 floats) between the two bias copies
 
 constexpr float kLog2e = 1.4426950408889634f;
@@ -229,7 +233,7 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // Resident bias rows, filled cooperatively by warps 2-3 and 12-15 (192 threads).
+  // Resident bias rows, filled cooperatively by warps 2 and 4-15 (kRowFillers threads).
   auto fill_rows = [&](int tid) {
     const int two_s = 2 * a.S - 1;
     const float* pdh = a.pd + (size_t)h * two_s;
@@ -237,8 +241,7 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
     const int n = (int)rev_row_floats(a.S);
     const int top = m_top + kRevPad;   // rev[i] = pd[top - i]
     const int lo = max(0, m_top - (nq * kBlk + kBlk - 2)), hi = min(two_s - 1, m_top);
-    attn::fill_row_rev(rev0, n, top, pdh, lo, hi, kLog2e, tid, kRowFillers);
-    attn::fill_row_rev(rev1, n, top - 1, pdh, lo, hi, kLog2e, tid, kRowFillers);
+    attn::fill_row_rev2(rev0, rev1, n, top, pdh, lo, hi, kLog2e, tid, kRowFillers);
     mbar_arrive(row_full);
   };
 
@@ -309,9 +312,8 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
       }
     }
   } else if (warp == 2) {
-    if constexpr (RES) fill_rows(threadIdx.x - 64);
+    if constexpr (RES) fill_rows(filler_id());
   } else if (warp == 3) {
-    if constexpr (RES) fill_rows(threadIdx.x - 64);
     // ------------------------------------------------------------ stage finisher
     // Publishes each stage once its TMA loads have landed, after writing the block's per-query
     // vectors (unfolded) or the padding columns (folded) and, when the bias row is not resident,
@@ -498,7 +500,7 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
   }
   } else if (warp < 12) {
     regs_inc<kRegsCompute>();
-    if constexpr (RES) fill_rows(threadIdx.x - 64);
+    if constexpr (RES) fill_rows(filler_id());
     // ------------------------------------------------------------ compute: one key x 64 queries per thread
     const int quarter = warp % 4, half = (warp - 4) / 4;
     const int kr = quarter * 32 + lane;        // key row within the block (TMEM lane)
@@ -643,7 +645,7 @@ relpos_bwd_main_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_co
     }
   } else {
     regs_dec<kRegsDq>();
-    if constexpr (RES) fill_rows(threadIdx.x - 64);
+    if constexpr (RES) fill_rows(filler_id());
     // ------------------------------------------------------------ dQ WG: one query row per thread
     const int quarter = warp % 4;
     const int r = quarter * 32 + lane;

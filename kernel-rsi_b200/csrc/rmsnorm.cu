@@ -149,7 +149,8 @@ template <int XT, int WT, int TPR, int VEC, int NCH>
 __global__ void __launch_bounds__(RowCfg<TPR>::kThreads, kBwdMinBlocks<TPR, VEC, NCH>)
 rms_bwd_kernel(const typename Elem<XT>::T* __restrict__ g, const typename Elem<XT>::T* __restrict__ x,
                const typename Elem<WT>::T* __restrict__ w, const float* __restrict__ rstd,
-               typename Elem<XT>::T* __restrict__ dx, float* __restrict__ dw_part, int64_t rows, int n) {
+               typename Elem<XT>::T* __restrict__ dx, float* __restrict__ dw_part, int64_t rows, int n,
+               const typename Elem<XT>::T* __restrict__ gadd) {
   pdl_enter();
   using WE = Elem<WT>;
   using DE = Elem<Promote<XT, WT>::value>;   // dtype of the g*w product
@@ -270,6 +271,12 @@ rms_bwd_kernel(const typename Elem<XT>::T* __restrict__ g, const typename Elem<X
           float o[VEC];
 #pragma unroll
           for (int e = 0; e < VEC; ++e) o[e] = r * dn[c][e] - xv[c][e] * k;
+          if (gadd != nullptr) {   // a second gradient of x (a residual branch), added before rounding
+            float ga[VEC];
+            load_vec<XT, VEC>(gadd + row * n + col, ga, true);
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) o[e] += ga[e];
+          }
           store_vec<XT, VEC>(dxr + col, o);
         }
       }
@@ -398,7 +405,7 @@ struct FwdArgs {
 };
 struct BwdArgs {
   const void* g; const void* x; const void* w; const float* rstd; void* dx; void* dw; float* part;
-  int64_t nblocks; int64_t rows; int n; cudaStream_t s;
+  int64_t nblocks; int64_t rows; int n; cudaStream_t s; const void* gadd = nullptr;
 };
 
 template <int XT, int WT, int TPR, int VEC, int NCH>
@@ -425,7 +432,7 @@ int run_bwd(const BwdArgs& a) {
   KRSI_CUDA_TRY(launch_pdl(kern, dim3((unsigned)a.nblocks), dim3(Cfg::kThreads), smem, a.s,
                            (const typename Elem<XT>::T*)a.g, (const typename Elem<XT>::T*)a.x,
                            (const typename Elem<WT>::T*)a.w, a.rstd, (typename Elem<XT>::T*)a.dx, a.part, a.rows,
-                           a.n));
+                           a.n, (const typename Elem<XT>::T*)a.gadd));
   KRSI_CUDA_TRY(launch_pdl(rms_dw_reduce_kernel<WT>, dim3((unsigned)((a.n + 127) / 128)), dim3(kRedWarps * 32), 0, a.s,
                            (const float*)a.part, (typename Elem<WT>::T*)a.dw, (int)a.nblocks, a.n));
   return KRSI_OK;
@@ -500,9 +507,11 @@ extern "C" int krsi_rmsnorm_bwd_workspace_size(int64_t rows, int64_t n, size_t* 
   return KRSI_OK;
 }
 
-extern "C" int krsi_rmsnorm_bwd(const void* g, const void* x, const void* w, const float* rstd, void* dx, void* dw,
-                                void* workspace, size_t workspace_bytes, int64_t rows, int64_t n, int x_dtype,
-                                int w_dtype, cudaStream_t stream) {
+namespace krsi {
+namespace {
+int rmsnorm_bwd_impl(const void* g, const void* x, const void* w, const float* rstd, const void* gadd, void* dx,
+                     void* dw, void* workspace, size_t workspace_bytes, int64_t rows, int64_t n, int x_dtype,
+                     int w_dtype, cudaStream_t stream) {
   KRSI_CHECK_ARG(rows >= 0 && n >= 0 && dtype_ok(x_dtype) && dtype_ok(w_dtype));
   if (n == 0) return KRSI_OK;
   KRSI_CHECK_ARG(w && dw);
@@ -518,8 +527,27 @@ extern "C" int krsi_rmsnorm_bwd(const void* g, const void* x, const void* w, con
   if (!plan_rows(n, x_dtype, vec_ok, &p)) return KRSI_ERR_UNSUPPORTED;
   const int64_t nblocks = bwd_blocks(rows, p);
   if (!workspace || workspace_bytes < (size_t)nblocks * (size_t)n * sizeof(float)) return KRSI_ERR_WORKSPACE;
+  if (gadd && p.vec > 1 && !aligned16(gadd)) return KRSI_ERR_MISALIGNED;
   return dispatch<false>(x_dtype, w_dtype, p,
-                         BwdArgs{g, x, w, rstd, dx, dw, static_cast<float*>(workspace), nblocks, rows, (int)n, stream});
+                         BwdArgs{g, x, w, rstd, dx, dw, static_cast<float*>(workspace), nblocks, rows, (int)n, stream,
+                                 gadd});
+}
+}  // namespace
+}  // namespace krsi
+
+extern "C" int krsi_rmsnorm_bwd(const void* g, const void* x, const void* w, const float* rstd, void* dx, void* dw,
+                                void* workspace, size_t workspace_bytes, int64_t rows, int64_t n, int x_dtype,
+                                int w_dtype, cudaStream_t stream) {
+  return rmsnorm_bwd_impl(g, x, w, rstd, nullptr, dx, dw, workspace, workspace_bytes, rows, n, x_dtype, w_dtype,
+                          stream);
+}
+
+extern "C" int krsi_rmsnorm_bwd_add(const void* g, const void* x, const void* w, const float* rstd, const void* gadd,
+                                    void* dx, void* dw, void* workspace, size_t workspace_bytes, int64_t rows,
+                                    int64_t n, int x_dtype, int w_dtype, cudaStream_t stream) {
+  if (rows > 0 && n > 0) KRSI_CHECK_ARG(gadd);
+  return rmsnorm_bwd_impl(g, x, w, rstd, gadd, dx, dw, workspace, workspace_bytes, rows, n, x_dtype, w_dtype,
+                          stream);
 }
 
 // ---------------------------------------------------------------- allocation-free backward

@@ -79,6 +79,33 @@ std::tuple<at::Tensor, at::Tensor> rmsnorm_bwd(const at::Tensor& g_in, const at:
   return {dx, dw};
 }
 
+std::tuple<at::Tensor, at::Tensor> rmsnorm_bwd_add(const at::Tensor& g_in, const at::Tensor& x2d_in,
+                                                   const at::Tensor& w_in, const at::Tensor& rstd_in,
+                                                   const at::Tensor& gadd_in) {
+  check_cuda(g_in, "g");
+  check_cuda(x2d_in, "x2d");
+  check_cuda(gadd_in, "gadd");
+  TORCH_CHECK(x2d_in.dim() == 2 && g_in.sizes() == x2d_in.sizes() && gadd_in.sizes() == x2d_in.sizes(),
+              "rmsnorm_bwd_add: g and gadd must match x2d");
+  TORCH_CHECK(rstd_in.scalar_type() == at::kFloat && rstd_in.numel() == x2d_in.size(0), "rmsnorm_bwd_add: bad rstd");
+  c10::cuda::CUDAGuard guard(x2d_in.device());
+  auto x2d = x2d_in.contiguous();
+  auto g = g_in.to(x2d.scalar_type()).contiguous();
+  auto gadd = gadd_in.to(x2d.scalar_type()).contiguous();
+  auto w = w_in.contiguous();
+  auto rstd = rstd_in.contiguous();
+  auto dx = at::empty_like(x2d);
+  auto dw = at::empty_like(w);
+  size_t ws = 0;
+  check_rc(krsi_rmsnorm_bwd_workspace_size(x2d.size(0), x2d.size(1), &ws), "krsi_rmsnorm_bwd_workspace_size");
+  auto wsp = workspace(x2d, ws);
+  check_rc(krsi_rmsnorm_bwd_add(g.data_ptr(), x2d.data_ptr(), w.data_ptr(), rstd.data_ptr<float>(), gadd.data_ptr(),
+                                dx.data_ptr(), dw.data_ptr(), wsp.data_ptr(), (size_t)wsp.numel(), x2d.size(0),
+                                x2d.size(1), krsi_dtype_of(x2d), krsi_dtype_of(w), at::cuda::getCurrentCUDAStream()),
+           "krsi_rmsnorm_bwd_add");
+  return {dx, dw};
+}
+
 // ---------------------------------------------------------------- GEGLU
 at::Tensor geglu_fwd(const at::Tensor& u_in) {
   check_cuda(u_in, "u");
@@ -212,6 +239,7 @@ at::Tensor t5_bias_bwd(const at::Tensor& dpd_in, const at::Tensor& table, int64_
 TORCH_LIBRARY(krsi, m) {
   m.def("rmsnorm_fwd(Tensor x2d, Tensor w, float eps) -> (Tensor, Tensor)");
   m.def("rmsnorm_bwd(Tensor g, Tensor x2d, Tensor w, Tensor rstd) -> (Tensor, Tensor)");
+  m.def("rmsnorm_bwd_add(Tensor g, Tensor x2d, Tensor w, Tensor rstd, Tensor gadd) -> (Tensor, Tensor)");
   m.def("geglu_fwd(Tensor u) -> Tensor");
   m.def("geglu_bwd(Tensor g, Tensor u) -> Tensor");
   m.def("relpos_attn_fwd(Tensor qkv, Tensor pd, int B, int S, int H, int D, float scale) -> (Tensor, Tensor, Tensor)");
@@ -224,6 +252,7 @@ TORCH_LIBRARY(krsi, m) {
 TORCH_LIBRARY_IMPL(krsi, CUDA, m) {
   m.impl("rmsnorm_fwd", &rmsnorm_fwd);
   m.impl("rmsnorm_bwd", &rmsnorm_bwd);
+  m.impl("rmsnorm_bwd_add", &rmsnorm_bwd_add);
   m.impl("geglu_fwd", &geglu_fwd);
   m.impl("geglu_bwd", &geglu_bwd);
   m.impl("relpos_attn_fwd", &relpos_attn_fwd);

@@ -95,6 +95,36 @@ class BlockConfig:
         return 6 * self.linear_params() + 12 * self.seq * self.heads * self.head_dim * self.layers
 
 
+class _RMSNormSkip(torch.autograd.Function):
+    """(rmsnorm(x, w, eps), x) for a pre-norm residual block, where x feeds both the norm and the
+    residual branch: the backward gets both gradients of x at once and adds them inside the RMSNorm
+    backward kernel (krsi::rmsnorm_bwd_add) instead of in a separate autograd pass over x."""
+
+    @staticmethod
+    def forward(ctx, x2d, w, eps):
+        y, rstd = torch.ops.krsi.rmsnorm_fwd(x2d, w, eps)
+        ctx.save_for_backward(x2d, w, rstd)
+        return y, x2d.view_as(x2d)
+
+    @staticmethod
+    def backward(ctx, gy, gskip):
+        x2d, w, rstd = ctx.saved_tensors
+        if gy is None:
+            return gskip, None, None
+        if gskip is None:
+            dx, dw = torch.ops.krsi.rmsnorm_bwd(gy.contiguous(), x2d, w, rstd)
+        else:
+            dx, dw = torch.ops.krsi.rmsnorm_bwd_add(gy.contiguous(), x2d, w, rstd, gskip.contiguous())
+        return dx, dw, None
+
+
+def _norm_and_skip(ops, x2, w, eps):
+    """The normalised rows and the residual input: fused when `ops` runs on the B200 kernels."""
+    if getattr(ops, "fused_norm_skip", False):
+        return _RMSNormSkip.apply(x2, w, eps)
+    return ops.rmsnorm(x2, w, eps), x2
+
+
 class Layer(nn.Module):
     def __init__(self, cfg: BlockConfig, ops, gen: torch.Generator, device, dtype=torch.bfloat16):
         super().__init__()
@@ -119,7 +149,7 @@ class Layer(nn.Module):
         cfg, ops = self.cfg, self.ops
         B, L, d = x.shape
         x2 = x.reshape(B * L, d)
-        h = ops.rmsnorm(x2, self.norm1, cfg.eps)
+        h, x2 = _norm_and_skip(ops, x2, self.norm1, cfg.eps)
         qkv = _Linear.apply(h, self.wqkv, None)
         marks = self.attn_marks
         if marks is not None:           # fwd begin / bwd end
@@ -128,7 +158,7 @@ class Layer(nn.Module):
         if marks is not None:           # fwd end / bwd begin
             a = _Mark.apply(a, marks[1], marks[2])
         x2 = _Linear.apply(a, self.wo, x2)          # residual add inside the GEMM (beta = 1)
-        h = ops.rmsnorm(x2, self.norm2, cfg.eps)
+        h, x2 = _norm_and_skip(ops, x2, self.norm2, cfg.eps)
         g = ops.geglu(_Linear.apply(h, self.wi, None))
         x2 = _Linear.apply(g, self.wo2, x2)
         return x2.reshape(B, L, d)
@@ -206,3 +236,5 @@ class LibraryOps:
         self.rmsnorm = rmsnorm.rmsnorm
         self.geglu = geglu.geglu
         self.relpos_attention = relpos_attention.relpos_attention
+        # RMSNorm and the residual branch share their input: one backward kernel adds both gradients
+        self.fused_norm_skip = True

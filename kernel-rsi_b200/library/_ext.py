@@ -84,6 +84,10 @@ def _register_compile_support() -> None:
     def _(g, x2d, w, rstd):
         return torch.empty_like(x2d), torch.empty_like(w)
 
+    @reg_fake("krsi::rmsnorm_bwd_add")
+    def _(g, x2d, w, rstd, gadd):
+        return torch.empty_like(x2d), torch.empty_like(w)
+
     @reg_fake("krsi::geglu_fwd")
     def _(u):
         return u.new_empty((u.shape[0], u.shape[1] // 2))

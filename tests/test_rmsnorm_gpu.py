@@ -149,3 +149,16 @@ def test_compile_fullgraph():
     y, r = torch.ops.krsi.rmsnorm_fwd(x, w, 1e-6)
     dx, _ = torch.ops.krsi.rmsnorm_bwd(g, x, w, r)
     assert torch.equal(out, y) and torch.equal(gx, dx)
+
+
+@pytest.mark.parametrize("rows,n,dt", [(300, 1152, torch.bfloat16), (64, 1000, torch.float32), (33, 17, torch.float16)])
+def test_bwd_add_is_the_backward_plus_the_added_gradient(rows, n, dt):
+    """krsi::rmsnorm_bwd_add (the block's fused residual gradient): dw unchanged, dx = dx + gadd."""
+    x, w, g = (t.to(dev, dt) for t in O.rmsnorm_inputs(rows, n, torch.float32, seed=rows))
+    gadd = torch.randn(rows, n, device=dev).to(dt)
+    _, rstd = torch.ops.krsi.rmsnorm_fwd(x, w, 1e-6)
+    dx, dw = torch.ops.krsi.rmsnorm_bwd(g, x, w, rstd)
+    dx2, dw2 = torch.ops.krsi.rmsnorm_bwd_add(g, x, w, rstd, gadd)
+    assert torch.equal(dw, dw2)
+    tol = 1e-6 if dt == torch.float32 else 1e-2
+    assert norm_max_err(dx2.float(), dx.float() + gadd.float()) <= tol
