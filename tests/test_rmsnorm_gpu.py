@@ -19,7 +19,8 @@ def krsi():
 
 def test_baseline_config_fp32_max_abs_1e5():
     """Config 1: x [2,1024,1152] fp32 ~ N(0,1), w = 1 + N(0,0.02), eps 1e-6, g ~ N(0,1):
-    output and both gradients within max-abs 1e-5 of the fp32 reference path."""
+    output, rstd and dx within max-abs 1e-5 of the fp64 oracle; dw (a sum of 2048 rows) within the
+    reference fp32 path's own max-abs error and 1e-5 of its magnitude."""
     x, w, g = O.rmsnorm_inputs(2048, 1152, torch.float32, seed=0)
     xd, wd, gd = x.to(dev), w.to(dev), g.to(dev)
     y, rstd = torch.ops.krsi.rmsnorm_fwd(xd, wd, 1e-6)
@@ -29,8 +30,14 @@ def test_baseline_config_fp32_max_abs_1e5():
     assert max_abs_err(y.cpu(), y_o) <= 1e-5
     assert max_abs_err(rstd.cpu(), r_o) <= 1e-5
     assert max_abs_err(dx.cpu(), dx_o) <= 1e-5
-    # dw sums 2048 rows: compare against the fp64 oracle relative to its magnitude
+    # dw sums 2048 rows (|dw| up to ~140): max-abs 1e-5 is below fp32 summation rounding.  The
+    # reference's own fp32 path misses it too (2.4e-5 here); the kernel must stay within 1e-5
+    # relative to dw's magnitude and within the reference path's own max-abs error.
+    _, dw64 = O.rmsnorm_bwd(g.double(), x.double(), w.double(), r_o)
+    xr0, wr0 = x.clone().requires_grad_(True), w.clone().requires_grad_(True)
+    _, dw_ref32 = torch.autograd.grad(O.rmsnorm_reference(xr0, wr0, 1e-6), [xr0, wr0], g)
     assert norm_max_err(dw.cpu(), dw_o) <= 1e-5
+    assert max_abs_err(dw.cpu(), dw64) <= max(1e-5, max_abs_err(dw_ref32, dw64))
     # through the autograd Function, against the reference's eager expression in fp32
     xr = xd.clone().requires_grad_(True)
     wr = wd.clone().requires_grad_(True)
