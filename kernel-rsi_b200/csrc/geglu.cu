@@ -25,26 +25,12 @@ struct GeluParts {
   float t, gel;
 };
 
-// 1/d for d in [1, inf) on the FMA pipe, which these kernels leave mostly idle, instead of the SFU
-// (the XU pipe carries the exponential and every float-to-16-bit conversion and bounds the forward):
-// an integer-subtraction first guess (relative error < 1/8) and three Newton steps
-// x <- x (2 - d x), each squaring the error: below 1e-7 relative, as the SFU's approximate reciprocal.
-// d is clamped so that e = inf (large z) still gives 1/d ~ 0.
-__device__ __forceinline__ float rcp_newton(float d) {
-  d = fminf(d, 1e30f);
-  float x = __int_as_float(0x7ef311c3 - __float_as_int(d));
-  x = x * fmaf(-d, x, 2.0f);
-  x = x * fmaf(-d, x, 2.0f);
-  x = x * fmaf(-d, x, 2.0f);
-  return x;
-}
-
 __device__ __forceinline__ GeluParts gelu_parts(float a) {
   const float z = kSqrt2OverPi * (a + kGeluC * a * a * a);
-  // exp(2z) on the SFU (the reference's tl.exp), the division on the FMA pipe;
+  // exp(2z) and the reciprocal on the SFU (the reference's tl.exp and approximate division);
   // 1 - 2/(e+1) saturates to +-1 for large |z| (e = inf or 0).
   const float e = ex2_approx(2.0f * kLog2e * z);
-  const float t = fmaf(-2.0f, rcp_newton(e + 1.0f), 1.0f);
+  const float t = fmaf(-2.0f, rcp_approx(e + 1.0f), 1.0f);
   return {t, 0.5f * a * (1.0f + t)};
 }
 
