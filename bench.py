@@ -157,6 +157,7 @@ class OpWorkload:
 
     def __init__(self, rank: int, world: int):
         self.rank, self.world = rank, world
+        self.copies = max(2, min(MAX_COPIES, math.ceil(3 * L2_BYTES / max(self.in_bytes, 1))))
 
     @property
     def work(self):
@@ -168,7 +169,6 @@ class OpWorkload:
 
     def setup(self, dev):
         self.setup_host()
-        self.copies = max(2, min(MAX_COPIES, math.ceil(3 * L2_BYTES / max(self.in_bytes, 1))))
         self.dev_inputs = [tuple(t.to(dev) for t in self.host) for _ in range(self.copies)]
         self.e2e_in = tuple(t.pin_memory() for t in self.host)
         self.capture()
@@ -753,8 +753,7 @@ def run_reference_arm(args, rank, world):
     line = {"impl": "reference", "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / max(args.steps, 1),
             "higher_is_better": wl.higher_is_better, "scaling": wl.scaling, "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded)", "config": {"workload": wl.config()["workload"]} if args.workload != "block"
-            else wl.config(),
+            "data": "synthetic (seeded)", "config": wl.config(),
             "cpu_baseline": {"value": value, "unit": wl.unit, "cores": threads, "kind": "port",
                              "sample": f"{args.steps} x {desc} on {cpu_info()}"},
             "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}

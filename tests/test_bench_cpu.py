@@ -1,0 +1,37 @@
+"""bench.py on the CPU: the reference arm's JSON line (the driver's contract) on a small workload,
+and the rule that the GPU arm imports the oracle only in its CPU-baseline leg (cpu_sample)."""
+import ast
+import json
+import subprocess
+import sys
+
+from conftest import ROOT
+
+
+def test_reference_arm_prints_one_contract_line():
+    p = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--workload", "rmsnorm",
+                        "--steps", "2", "--warmup", "3"], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert p.returncode == 0, p.stderr[-2000:]
+    lines = [l for l in p.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["value"] > 0 and d["unit"] == "GB/s"
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["cpu_baseline"]["kind"] == "port"
+    for key in ("metric", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling", "dtype",
+                "config"):
+        assert key in d
+
+
+def test_oracle_only_in_the_cpu_baseline_leg():
+    tree = ast.parse((ROOT / "bench.py").read_text())
+    allowed = {"cpu_sample"}
+
+    def imports_oracle(node):
+        return any((isinstance(n, ast.ImportFrom) and (n.module or "").startswith("oracle")) or
+                   (isinstance(n, ast.Import) and any(a.name.startswith("oracle") for a in n.names))
+                   for n in ast.walk(node))
+
+    assert not any(imports_oracle(n) for n in tree.body if not isinstance(n, (ast.FunctionDef, ast.ClassDef)))
+    for node in ast.walk(tree):
+        if isinstance(node, ast.FunctionDef) and imports_oracle(node):
+            assert node.name in allowed, node.name
