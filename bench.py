@@ -849,6 +849,12 @@ def run_profile_case(which: str, n: int, S: int | None):
             u, g = (t.to(dev) for t in geglu_inputs(n, 4608, torch.bfloat16, seed=0))
             ops.geglu_fwd(u)
             ops.geglu_bwd(g, u)
+        elif which == "t5_bias":
+            H, nb = 16, 32
+            g = torch.Generator().manual_seed(0)
+            table = (0.5 * torch.randn(nb, H, generator=g)).to(dev)
+            pd = ops.t5_bias_fwd(table, n, nb, 128, True)
+            ops.t5_bias_bwd(torch.randn_like(pd), table, n, nb, 128, True)
         elif which in ("attn", "attn_fwd"):
             H, D = 16, 72
             qkv, pd, dout = (t.to(dev) for t in attn_inputs(n, S, H, D, torch.bfloat16, seed=0))
@@ -872,7 +878,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ops", action="store_true", help="block at N=1: skip the configs 1-4 `ops` object")
     ap.add_argument("--profile-case", nargs="+", metavar="ARG",
-                    help="KIND N [S]: rmsnorm|rmsnorm_bf16 ROWS, geglu ROWS, attn|attn_fwd B S")
+                    help="KIND N [S]: rmsnorm|rmsnorm_bf16 ROWS, geglu ROWS, attn|attn_fwd B S, t5_bias S")
     args = ap.parse_args()
     if args.profile_case:
         pc = args.profile_case

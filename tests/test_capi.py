@@ -64,3 +64,13 @@ def test_workspace_queries(lib):
     assert sz.value == 296 * 1152 * 4
     assert lib.krsi_rmsnorm_bwd_workspace_size(ctypes.c_int64(3), ctypes.c_int64(10), ctypes.byref(sz)) == 0
     assert sz.value == 3 * 10 * 4
+
+
+def test_rmsnorm_bwd_add_argument_checks():
+    """The fused residual-gradient RMSNorm backward rejects a missing added gradient before any
+    device work (the other checks are the plain backward's)."""
+    lib = ctypes.CDLL(str(PKG / "lib" / "libkrsi_b200.so"))
+    vp, i64 = ctypes.c_void_p, ctypes.c_int64
+    rc = lib.krsi_rmsnorm_bwd_add(vp(1), vp(1), vp(1), vp(1), vp(0), vp(1), vp(1), vp(1), ctypes.c_size_t(1 << 20),
+                                  i64(4), i64(8), 0, 0, vp(0))
+    assert rc == 1

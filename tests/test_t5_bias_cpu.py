@@ -72,3 +72,4 @@ def test_oracle_matches_the_torch_expression():
         t = table.clone().requires_grad_(True)
         (g,) = torch.autograd.grad(t5_bias.reference(t, 300, bi), [t], dpd.float())
         torch.testing.assert_close(O.t5_bias_bwd(dpd, 300, 6, bi), g.double(), rtol=1e-6, atol=1e-6)
+
