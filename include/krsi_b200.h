@@ -111,6 +111,16 @@ int krsi_geglu_fwd(const void* u, void* out, int64_t rows, int64_t F, int dtype,
 int krsi_geglu_bwd(const void* g, const void* u, void* du, int64_t rows, int64_t F,
                    int dtype, cudaStream_t stream);
 
+/* The gate|value projection with GEGLU in its epilogue (tcgen05 GEMM, fp32 accumulate):
+ *   u = x @ w^T (rounded to dtype), out = gelu_tanh(u[:, :F]).to(dtype) * u[:, F:]
+ * with krsi_geglu_fwd's arithmetic on the rounded u, so out equals krsi_geglu_fwd(u) bit for bit.
+ * Replaces the T5 feed-forward's `geglu(h @ wi.T)`: the projection followed by
+ * library/geglu.py:104-108 (geglu -> _fwd, geglu.py:55-61 -> _geglu_fwd, geglu.py:27-35).
+ * x: [rows, K]; w: [2F, K] (rows [0, F) gate, [F, 2F) value); u: [rows, 2F]; out: [rows, F];
+ * all of `dtype` (BF16 or F16), contiguous, 16-byte aligned; K and F multiples of 8. */
+int krsi_linear_geglu_fwd(const void* x, const void* w, void* u, void* out, int64_t rows,
+                          int64_t K, int64_t F, int dtype, cudaStream_t stream);
+
 /* ---------------------------------------------------------------- relpos attention
  * Flash attention with an additive Toeplitz bias, non-causal:
  *   s2[i,j] = (q_i . k_j * scale + pd[h, j-i+S-1]) * log2(e),  p = softmax over j,

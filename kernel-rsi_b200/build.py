@@ -27,7 +27,8 @@ LIB = PKG / "lib"
 CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 NVCC = str(CUDA_HOME / "bin" / "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CU_SOURCES = ["capi.cu", "diag.cu", "rmsnorm.cu", "geglu.cu", "relpos_attn_fwd.cu", "relpos_attn_bwd.cu", "t5_bias.cu"]
+CU_SOURCES = ["capi.cu", "diag.cu", "rmsnorm.cu", "geglu.cu", "relpos_attn_fwd.cu", "relpos_attn_bwd.cu", "t5_bias.cu",
+              "linear_geglu.cu"]
 C_ABI_LIB = LIB / "libkrsi_b200.so"
 TORCH_LIB = LIB / "_krsi_torch.so"
 

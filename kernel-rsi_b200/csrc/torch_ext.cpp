@@ -136,6 +136,26 @@ at::Tensor geglu_bwd(const at::Tensor& g_in, const at::Tensor& u_in) {
   return du;
 }
 
+// ---------------------------------------------------------------- projection + GEGLU
+std::tuple<at::Tensor, at::Tensor> linear_geglu_fwd(const at::Tensor& x_in, const at::Tensor& w_in) {
+  check_cuda(x_in, "x2d");
+  check_cuda(w_in, "w");
+  TORCH_CHECK(x_in.dim() == 2, "linear_geglu: x2d must be 2-D, got ", x_in.dim(), "-D");
+  TORCH_CHECK(w_in.dim() == 2 && w_in.size(1) == x_in.size(1) && w_in.size(0) % 2 == 0,
+              "linear_geglu: w must be [2F, ", x_in.size(1), "]");
+  TORCH_CHECK(x_in.scalar_type() == w_in.scalar_type(), "linear_geglu: x2d and w must have one dtype");
+  c10::cuda::CUDAGuard guard(x_in.device());
+  auto x = x_in.contiguous();
+  auto w = w_in.contiguous();
+  const int64_t F = w.size(0) / 2;
+  auto u = at::empty({x.size(0), 2 * F}, x.options());
+  auto out = at::empty({x.size(0), F}, x.options());
+  check_rc(krsi_linear_geglu_fwd(x.data_ptr(), w.data_ptr(), u.data_ptr(), out.data_ptr(), x.size(0), x.size(1), F,
+                                 krsi_dtype_of(x), at::cuda::getCurrentCUDAStream()),
+           "krsi_linear_geglu_fwd");
+  return {u, out};
+}
+
 // ---------------------------------------------------------------- relpos attention
 void check_attn_shapes(const at::Tensor& qkv, const at::Tensor& pd, int64_t B, int64_t S, int64_t H, int64_t D) {
   TORCH_CHECK(B >= 0 && S >= 0 && H > 0 && D > 0, "relpos_attention: bad B/S/H/D");
@@ -242,6 +262,7 @@ TORCH_LIBRARY(krsi, m) {
   m.def("rmsnorm_bwd_add(Tensor g, Tensor x2d, Tensor w, Tensor rstd, Tensor gadd) -> (Tensor, Tensor)");
   m.def("geglu_fwd(Tensor u) -> Tensor");
   m.def("geglu_bwd(Tensor g, Tensor u) -> Tensor");
+  m.def("linear_geglu_fwd(Tensor x2d, Tensor w) -> (Tensor, Tensor)");
   m.def("relpos_attn_fwd(Tensor qkv, Tensor pd, int B, int S, int H, int D, float scale) -> (Tensor, Tensor, Tensor)");
   m.def("relpos_attn_bwd(Tensor dout, Tensor qkv, Tensor pd, Tensor out32, Tensor lse, int B, int S, int H, int D, "
         "float scale) -> (Tensor, Tensor)");
@@ -255,6 +276,7 @@ TORCH_LIBRARY_IMPL(krsi, CUDA, m) {
   m.impl("rmsnorm_bwd_add", &rmsnorm_bwd_add);
   m.impl("geglu_fwd", &geglu_fwd);
   m.impl("geglu_bwd", &geglu_bwd);
+  m.impl("linear_geglu_fwd", &linear_geglu_fwd);
   m.impl("relpos_attn_fwd", &relpos_attn_fwd);
   m.impl("relpos_attn_bwd", &relpos_attn_bwd);
   m.impl("t5_bias_fwd", &t5_bias_fwd);

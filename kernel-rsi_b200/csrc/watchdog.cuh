@@ -18,6 +18,9 @@ enum WatchdogRole : unsigned {
   kWdBwdMma = 10,
   kWdBwdCompute = 11,
   kWdBwdDq = 12,
+  kWdGemmLoad = 17,   // fused projection GEMM: TMA producer waiting for a free stage
+  kWdGemmMma = 18,    // fused projection GEMM: MMA issuer waiting for data / a free accumulator
+  kWdGemmEpilogue = 19,
   kWdTest = 0x7f      // the self-test kernel's deliberately unsatisfied wait
 };
 
@@ -30,15 +33,18 @@ constexpr unsigned kSpinLimit = 1u << 22;
 cudaError_t watchdog_read_attn_fwd(unsigned* word, bool clear);
 cudaError_t watchdog_read_attn_bwd(unsigned* word, bool clear);
 cudaError_t watchdog_read_diag(unsigned* word, bool clear);
+cudaError_t watchdog_read_gemm(unsigned* word, bool clear);
 
 inline cudaError_t watchdog_read(unsigned* word, bool clear) {
-  unsigned a = 0, b = 0, c = 0;
+  unsigned a = 0, b = 0, c = 0, d = 0;
   cudaError_t e = watchdog_read_attn_fwd(&a, clear);
   if (e != cudaSuccess) return e;
   e = watchdog_read_attn_bwd(&b, clear);
   if (e != cudaSuccess) return e;
   e = watchdog_read_diag(&c, clear);
-  *word = a | b | c;
+  if (e != cudaSuccess) return e;
+  e = watchdog_read_gemm(&d, clear);
+  *word = a | b | c | d;
   return e;
 }
 

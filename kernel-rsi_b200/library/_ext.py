@@ -1,9 +1,10 @@
 """Loader for the krsi_b200 native libraries, plus the compile-path glue of the krsi::* ops.
 
 The CUDA kernels live in lib/libkrsi_b200.so (C ABI, include/krsi_b200.h); lib/_krsi_torch.so
-registers the operators krsi::rmsnorm_fwd/bwd, krsi::geglu_fwd/bwd and
-krsi::relpos_attn_fwd/bwd with the schemas of the reference's triton_ops
-(library/rmsnorm.py:86-103, library/geglu.py:85-101, library/relpos_attention.py:175-195).
+registers the operators krsi::rmsnorm_fwd/bwd, krsi::geglu_fwd/bwd and krsi::relpos_attn_fwd/bwd
+with the schemas of the reference's triton_ops (library/rmsnorm.py:86-103, library/geglu.py:85-101,
+library/relpos_attention.py:175-195), plus krsi::linear_geglu_fwd (the gate|value projection with
+the GEGLU forward in its epilogue) and the T5 bias ops, which have no reference operator.
 This module adds what torch.compile needs on top: fake (meta) implementations and
 register_autograd for each forward op.
 
@@ -96,6 +97,10 @@ def _register_compile_support() -> None:
     def _(g, u):
         return torch.empty_like(u)
 
+    @reg_fake("krsi::linear_geglu_fwd")
+    def _(x2d, w):
+        return x2d.new_empty((x2d.shape[0], w.shape[0])), x2d.new_empty((x2d.shape[0], w.shape[0] // 2))
+
     @reg_fake("krsi::relpos_attn_fwd")
     def _(qkv, pd, B, S, H, D, scale):
         return (qkv.new_empty((B * S, H * D)), qkv.new_empty((B * S, H * D), dtype=torch.float32),
@@ -133,6 +138,18 @@ def _register_compile_support() -> None:
         return ops.geglu_bwd(g.contiguous(), u)
 
     torch.library.register_autograd("krsi::geglu_fwd", geglu_backward, setup_context=geglu_setup)
+
+    def lg_setup(ctx, inputs, output):
+        ctx.save_for_backward(inputs[0], inputs[1], output[0])
+
+    def lg_backward(ctx, gu, gout):
+        x2d, w, u = ctx.saved_tensors
+        du = ops.geglu_bwd(gout.contiguous(), u)
+        if gu is not None:
+            du = du + gu
+        return du @ w, du.t() @ x2d
+
+    torch.library.register_autograd("krsi::linear_geglu_fwd", lg_backward, setup_context=lg_setup)
 
     def attn_setup(ctx, inputs, output):
         qkv, pd, B, S, H, D, scale = inputs

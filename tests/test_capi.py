@@ -74,3 +74,17 @@ def test_rmsnorm_bwd_add_argument_checks():
     rc = lib.krsi_rmsnorm_bwd_add(vp(1), vp(1), vp(1), vp(1), vp(0), vp(1), vp(1), vp(1), ctypes.c_size_t(1 << 20),
                                   i64(4), i64(8), 0, 0, vp(0))
     assert rc == 1
+
+
+def test_linear_geglu_argument_checks(lib):
+    """The fused projection + GEGLU refuses, before any device work: null pointers, fp32, a K or F
+    that is not a multiple of 8 (TMA row stride, 16-byte epilogue packets) and misaligned buffers;
+    zero rows is a no-op."""
+    vp, i64 = ctypes.c_void_p, ctypes.c_int64
+    call = lib.krsi_linear_geglu_fwd
+    assert call(vp(0), vp(16), vp(16), vp(16), i64(4), i64(64), i64(64), 1, vp(0)) == 1
+    assert call(vp(16), vp(16), vp(16), vp(16), i64(4), i64(64), i64(64), 0, vp(0)) == 2
+    assert call(vp(16), vp(16), vp(16), vp(16), i64(4), i64(60), i64(64), 1, vp(0)) == 2
+    assert call(vp(16), vp(16), vp(16), vp(16), i64(4), i64(64), i64(20), 1, vp(0)) == 2
+    assert call(vp(18), vp(16), vp(16), vp(16), i64(4), i64(64), i64(64), 1, vp(0)) == 3
+    assert call(vp(0), vp(0), vp(0), vp(0), i64(0), i64(64), i64(64), 1, vp(0)) == 0

@@ -1,0 +1,120 @@
+"""The gate|value projection with GEGLU in its epilogue (tcgen05 GEMM) vs the oracle, the standalone
+GEGLU kernel and the reference's criterion (B200)."""
+import ctypes
+
+import pytest
+import torch
+
+from gpu_util import DT, capi, ptr, reference_compare, stream
+from oracle import ops as O
+from oracle.compare import norm_max_err
+
+pytestmark = pytest.mark.gpu
+dev = "cuda"
+
+
+def krsi():
+    import linear_geglu
+    return linear_geglu
+
+
+def inputs(rows, K, F, dt, seed):
+    """x ~ N(0, 1) [rows, K], w ~ N(0, 1/K) [2F, K] (unit-variance u), g ~ N(0, 1) [rows, F]."""
+    x = O.gen((rows, K), seed)
+    w = O.gen((2 * F, K), seed + 1, std=K ** -0.5)
+    g = O.gen((rows, F), seed + 2)
+    return x.to(dt), w.to(dt), g.to(dt)
+
+
+@pytest.mark.parametrize("rows,K,F,dt", [
+    (2048, 1152, 4608, torch.bfloat16),   # the block's feed-forward: d 1152 -> 2 x 4608
+    (300, 1152, 4608, torch.bfloat16),    # ragged last row tile
+    (1, 64, 8, torch.bfloat16),           # one row, one partial F tile
+    (129, 72, 200, torch.bfloat16),       # K not a multiple of 64, F not a multiple of 128
+    (257, 1000, 136, torch.bfloat16),
+    (512, 768, 2048, torch.float16),      # T5 v1.1 base feed-forward, f16
+])
+def test_fused_vs_oracle_and_standalone_geglu(rows, K, F, dt):
+    x, w, _ = inputs(rows, K, F, dt, seed=rows + K + F)
+    u, out = torch.ops.krsi.linear_geglu_fwd(x.to(dev), w.to(dev))
+    u_o, out_o = O.linear_geglu_fwd(x, w)
+    # u: the fp32-accumulated product rounded once; the fp64 product rounded once differs by at most
+    # a rounding step where the two sums straddle a rounding boundary
+    assert norm_max_err(u.cpu(), u_o) <= 4e-3
+    assert (u.cpu() == u_o).float().mean().item() >= 0.99
+    # out: the GEGLU arithmetic on the kernel's own u, bit for bit the standalone GEGLU kernel
+    assert torch.equal(out, torch.ops.krsi.geglu_fwd(u))
+    assert norm_max_err(out.cpu(), out_o) <= 1e-2
+
+
+def test_autograd_vs_oracle():
+    rows, K, F = 512, 1152, 4608
+    x, w, g = inputs(rows, K, F, torch.bfloat16, seed=5)
+    xr = x.to(dev).requires_grad_(True)
+    wr = w.to(dev).requires_grad_(True)
+    out = krsi().linear_geglu(xr, wr)
+    dx, dw = torch.autograd.grad(out, [xr, wr], g.to(dev))
+    u, _ = torch.ops.krsi.linear_geglu_fwd(x.to(dev), w.to(dev))
+    dx_o, dw_o = O.linear_geglu_bwd(g, x, w, u.cpu())
+    assert norm_max_err(dx.cpu(), dx_o) <= 1e-2
+    assert norm_max_err(dw.cpu(), dw_o) <= 1e-2
+
+
+def test_reference_criterion_bf16():
+    """The reference's selftest criterion (compare() with slack 2 against the bf16 original) on the
+    T5 v1.1 base feed-forward shape, as linear_geglu.selftest() runs it."""
+    x, w, g = inputs(2048, 768, 2048, torch.float32, seed=9)
+    res, _, _ = reference_compare(krsi().linear_geglu, krsi().reference,
+                                  [x.to(dev, torch.bfloat16), w.to(dev, torch.bfloat16)], g.to(dev) * 1e-2)
+    assert res["pass"], res
+
+
+def test_deterministic_and_graph_capturable():
+    x, w, _ = inputs(1024, 1152, 4608, torch.bfloat16, seed=3)
+    x, w = x.to(dev), w.to(dev)
+    u1, o1 = torch.ops.krsi.linear_geglu_fwd(x, w)
+    u2, o2 = torch.ops.krsi.linear_geglu_fwd(x, w)
+    assert torch.equal(u1, u2) and torch.equal(o1, o2)
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        torch.ops.krsi.linear_geglu_fwd(x, w)
+    torch.cuda.current_stream().wait_stream(s)
+    with torch.cuda.graph(graph):
+        u3, o3 = torch.ops.krsi.linear_geglu_fwd(x, w)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(u3, u1) and torch.equal(o3, o1)
+    import _ext
+    assert _ext.device_status() == 0
+
+
+def test_compile_fullgraph():
+    x, w, g = (t.to(dev) for t in inputs(256, 512, 512, torch.bfloat16, seed=4))
+    fn = torch.compile(krsi().linear_geglu, fullgraph=True)
+    xr = x.clone().requires_grad_(True)
+    out = fn(xr, w)
+    (gx,) = torch.autograd.grad(out, [xr], g)
+    xe = x.clone().requires_grad_(True)
+    oe = krsi().linear_geglu(xe, w)
+    (ge,) = torch.autograd.grad(oe, [xe], g)
+    assert torch.equal(out, oe) and torch.equal(gx, ge)
+
+
+def test_c_abi_direct_call_and_errors():
+    lib = capi()
+    x, w, _ = (t.to(dev) for t in inputs(64, 256, 128, torch.bfloat16, seed=2))
+    u = torch.empty(64, 256, device=dev, dtype=torch.bfloat16)
+    out = torch.empty(64, 128, device=dev, dtype=torch.bfloat16)
+    args = (ctypes.c_int64(64), ctypes.c_int64(256), ctypes.c_int64(128), DT[torch.bfloat16], stream())
+    assert lib.krsi_linear_geglu_fwd(ptr(x), ptr(w), ptr(u), ptr(out), *args) == 0
+    torch.cuda.synchronize()
+    u2, o2 = torch.ops.krsi.linear_geglu_fwd(x, w)
+    assert torch.equal(u, u2) and torch.equal(out, o2)
+    # K not a multiple of 8 (TMA row stride), fp32 and a misaligned pointer are refused before launch
+    assert lib.krsi_linear_geglu_fwd(ptr(x), ptr(w), ptr(u), ptr(out), ctypes.c_int64(64), ctypes.c_int64(12),
+                                     ctypes.c_int64(128), DT[torch.bfloat16], stream()) == 2
+    assert lib.krsi_linear_geglu_fwd(ptr(x), ptr(w), ptr(u), ptr(out), ctypes.c_int64(64), ctypes.c_int64(256),
+                                     ctypes.c_int64(128), DT[torch.float32], stream()) == 2
+    assert lib.krsi_linear_geglu_fwd(ctypes.c_void_p(x.data_ptr() + 2), ptr(w), ptr(u), ptr(out), *args) == 3
