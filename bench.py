@@ -1,6 +1,7 @@
 """Benchmark of the krsi_b200 hot path on B200 (driver contract: one JSON line from rank 0).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload block|attn|attn_fwd|rmsnorm|geglu]
+  python bench.py [--gpus N] [--steps K] [--warmup W]
+                  [--workload block|attn|attn_fwd|rmsnorm|geglu|linear_geglu]
   python bench.py --impl reference ...      # the reference's torch CPU path on the host cores
   torchrun --nproc-per-node N bench.py --gpus N ...
   python bench.py --profile-case KIND N [S] # one small seeded case for a profiler (ncu), no timing
@@ -10,12 +11,16 @@ Workloads (all inputs synthetic, seeded, CPU-generated):
             +res -> RMSNorm -> wi GEMM -> GEGLU -> wo GEMM -> +res), x [32,1024,1152] bf16,
             fwd+bwd with loss = mean(out.float()^2); batch-sharded over N ranks, NCCL all-reduce of
             the weight gradients.  The whole training step (forward, backward, the bucketed
-            all-reduces) is one CUDA graph replay.  Metric: tok/s (whole job).  The default; at
-            N=1 its line also carries an `ops` object with configs 1-4 below.
+            all-reduces) is one CUDA graph replay; the wi GEMM and the GEGLU forward are one
+            kernel.  Metric: tok/s (whole job).  The default; at N=1 its line also carries an
+            `ops` object with configs 1-4 and linear_geglu below.
   attn      config 4: relpos attention fwd+bwd, B=8 H=16 L=2048 D=72 bf16. TFLOP/s (12*B*H*L^2*D).
   attn_fwd  config 3: relpos attention fwd, B=2 H=16 L=1024 D=72 bf16. TFLOP/s (4*B*H*L^2*D).
   rmsnorm   config 1: RMSNorm fwd+bwd fp32 [2048,1152]. GB/s (algorithmic bytes).
   geglu     config 2: GEGLU fwd+bwd bf16 [2048,9216]. GB/s (algorithmic bytes).
+  linear_geglu  one config-5 layer's gate|value projection with GEGLU in the GEMM epilogue,
+            x [32768,1152] @ wi [9216,1152]^T bf16, forward. TFLOP/s (2*rows*K*2F); the breakdown
+            times the unfused cuBLAS GEMM + GEGLU kernel on the same inputs.
 For the op workloads a step replays one CUDA graph holding C calls, one per rotating input copy
 (C copies > 3x the L2 cache, as the reference's time_calls rotates them); N>1 runs replicas.
 """
@@ -344,6 +349,88 @@ class GegluWorkload(RMSNormWorkload):
         return self.work_per_call, "one full fwd+bwd of config 2 (reference torch path, fp32 on CPU)"
 
 
+class LinearGegluWorkload(OpWorkload):
+    """The block's feed-forward input at one layer's shape: x [32768, 1152] @ wi [9216, 1152]^T with
+    GEGLU in the GEMM's epilogue (krsi::linear_geglu_fwd, one tcgen05 kernel), forward.  Tensor-bound:
+    the roofline is the GEMM's FLOPs against the measured bf16 peak.  The breakdown times the unfused
+    pair it replaces (cuBLAS GEMM, then the GEGLU kernel) on the same inputs."""
+    name, metric, unit, dtype = "linear_geglu", "gate|value projection + GEGLU forward throughput", "TFLOP/s", "bf16"
+    ROWS, K, F = 32768, 1152, 4608
+    work_per_call = 2 * ROWS * K * 2 * F
+    launches_per_call = 1
+    kernel_key = "linear_geglu_kernel"
+    in_bytes = (ROWS * K + 2 * F * K) * 2
+
+    def config(self):
+        return {"workload": "gate|value projection + GEGLU fwd, x[32768,1152] @ wi[9216,1152]^T bf16 (one config-5 "
+                            "layer's feed-forward input)", "rows": self.ROWS, "K": self.K, "F": self.F,
+                "l2": "rotating input copies > 3x L2 (u and out, 906 MB per call, are written fresh)",
+                "timing": f"one CUDA graph of {self.copies} calls per step"}
+
+    def setup_host(self):
+        from harness.inputs import gen
+
+        self.host = (gen((self.ROWS, self.K), 21, torch.bfloat16),
+                     gen((2 * self.F, self.K), 22, torch.bfloat16, std=0.02))
+
+    def call(self, x, w):
+        return torch.ops.krsi.linear_geglu_fwd(x, w)
+
+    def roofline(self, kms, pk):
+        t = kms / self.copies
+        ach = self.work_per_call / (t / 1e3) / 1e12
+        self._call_ms = t
+        return {"bound": "tensor", "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": ach / pk["bf16_tflops"], "traffic": ncu_traffic(self.kernel_key), "kernel": self.kernel_key,
+                "peak_source": pk["source"] + " (cuBLAS bf16 GEMM, burst: the kernel is timed alone)",
+                "per_launch_group": "one launch per call, device time per call from the graph replay"}
+
+    def breakdown(self, dev, kms):
+        """Device time per call of the unfused pair (cuBLAS GEMM + GEGLU kernel) and of the cuBLAS GEMM
+        alone, each as one CUDA graph over the same input copies."""
+        res = {}
+        for key, fn in (("unfused_ms_per_call", lambda x, w: torch.ops.krsi.geglu_fwd(x @ w.t())),
+                        ("cublas_gemm_ms_per_call", lambda x, w: x @ w.t())):
+            for inp in self.dev_inputs:
+                fn(*inp)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for inp in self.dev_inputs:
+                    fn(*inp)
+            g.replay()
+            torch.cuda.synchronize()
+            times = []
+            for _ in range(5):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                g.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                times.append(e0.elapsed_time(e1) / self.copies)
+            res[key] = statistics.median(times)
+            del g
+        return res
+
+    def extra(self):
+        b = {"ms_per_call": getattr(self, "_call_ms", None), "calls_per_step": self.copies}
+        b.update(getattr(self, "_breakdown", {}))
+        return {"breakdown": b}
+
+    def e2e_compute(self, inputs):
+        import linear_geglu
+
+        x, w = inputs
+        return [linear_geglu.linear_geglu(x, w)]
+
+    def cpu_sample(self):
+        x, w = self.host
+        rows = 256
+        gate, value = (x[:rows].float() @ w.float().t()).chunk(2, dim=-1)
+        torch.nn.functional.gelu(gate, approximate="tanh") * value
+        return 2 * rows * self.K * 2 * self.F, f"{rows} rows of the projection + GEGLU (reference torch path, fp32)"
+
+
 class AttnWorkload(OpWorkload):
     """Config 4: relpos attention fwd+bwd, B=8 H=16 L=2048 D=72 bf16 (training mode).  The C forward
     calls and the C backward calls are captured as two CUDA graphs, so the backward (the dominant
@@ -651,8 +738,8 @@ class BlockWorkload:
 
 
 WORKLOADS = {"rmsnorm": RMSNormWorkload, "geglu": GegluWorkload, "attn": AttnWorkload,
-             "attn_fwd": AttnFwdWorkload, "block": BlockWorkload}
-OPS_IN_DEFAULT_LINE = ("rmsnorm", "geglu", "attn_fwd", "attn")
+             "attn_fwd": AttnFwdWorkload, "linear_geglu": LinearGegluWorkload, "block": BlockWorkload}
+OPS_IN_DEFAULT_LINE = ("rmsnorm", "geglu", "attn_fwd", "attn", "linear_geglu")
 
 
 # ---------------------------------------------------------------- timing
@@ -849,6 +936,12 @@ def run_profile_case(which: str, n: int, S: int | None):
             u, g = (t.to(dev) for t in geglu_inputs(n, 4608, torch.bfloat16, seed=0))
             ops.geglu_fwd(u)
             ops.geglu_bwd(g, u)
+        elif which == "linear_geglu":
+            from harness.inputs import gen
+
+            x = gen((n, 1152), 21, torch.bfloat16).to(dev)
+            w = gen((2 * 4608, 1152), 22, torch.bfloat16, std=0.02).to(dev)
+            ops.linear_geglu_fwd(x, w)
         elif which == "t5_bias":
             H, nb = 16, 32
             g = torch.Generator().manual_seed(0)

@@ -121,6 +121,18 @@ int krsi_geglu_bwd(const void* g, const void* u, void* du, int64_t rows, int64_t
 int krsi_linear_geglu_fwd(const void* x, const void* w, void* u, void* out, int64_t rows,
                           int64_t K, int64_t F, int dtype, cudaStream_t stream);
 
+/* The down projection's input gradient with GEGLU's backward in its epilogue (tcgen05 GEMM):
+ *   g = dy @ w (fp32 accumulate, rounded to dtype; never written), du = geglu_bwd(g, u)
+ * with krsi_geglu_bwd's arithmetic, so du equals krsi_geglu_bwd(g, u) bit for bit for the rounded g.
+ * Replaces the backward of the T5 feed-forward's `geglu(h @ wi.T) @ wo.T` from the down projection's
+ * input gradient through GEGLU: `dy @ wo` followed by library/geglu.py:64-68 (_bwd -> _geglu_bwd,
+ * geglu.py:38-52).
+ * dy: [rows, K]; w: [K, F] (the down projection's weight, nn.Linear layout); u: [rows, 2F] (the
+ * gate|value projection's output); du: [rows, 2F]; all of `dtype` (BF16 or F16), contiguous,
+ * 16-byte aligned; K and F multiples of 8. */
+int krsi_linear_geglu_bwd(const void* dy, const void* w, const void* u, void* du, int64_t rows,
+                          int64_t K, int64_t F, int dtype, cudaStream_t stream);
+
 /* ---------------------------------------------------------------- relpos attention
  * Flash attention with an additive Toeplitz bias, non-causal:
  *   s2[i,j] = (q_i . k_j * scale + pd[h, j-i+S-1]) * log2(e),  p = softmax over j,

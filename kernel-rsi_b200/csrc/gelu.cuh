@@ -1,6 +1,7 @@
 // gelu.cuh - the GEGLU element arithmetic shared by the standalone GEGLU kernels (geglu.cu) and the
-// GEGLU epilogue of the fused projection GEMM (linear_geglu.cu), so both round at the same points
-// and produce identical bits from identical inputs.
+// GEGLU epilogues of the fused GEMMs (linear_geglu.cu: the gate|value projection's forward, the down
+// projection's input gradient), so all of them round at the same points and produce identical bits
+// from identical inputs.
 //
 // Semantics follow library/geglu.py of kernel-rsi:
 //   gelu parts (geglu.py:20-24): z = sqrt(2/pi)*(a + 0.044715 a^3);
@@ -39,14 +40,18 @@ __device__ __forceinline__ float geglu_out(float a, float b) {
   return E::round(E::round(gelu_parts(a).gel) * b);
 }
 
+// d(gate) from the gate value a, its tanh t and the rounded dgel = (g * b).to(dtype).
+__device__ __forceinline__ float geglu_dgate(float a, float t, float dgel) {
+  const float dz = kSqrt2OverPi * (1.0f + 3.0f * kGeluC * a * a);
+  return dgel * (0.5f * (1.0f + t) + 0.5f * a * (1.0f - t * t) * dz);
+}
+
 template <int DT>
 __device__ __forceinline__ void geglu_grad(float a, float b, float g, float* da, float* db) {
   using E = Elem<DT>;
   const GeluParts p = gelu_parts(a);
   *db = E::round(g * E::round(p.gel));
-  const float dgel = E::round(g * b);
-  const float dz = kSqrt2OverPi * (1.0f + 3.0f * kGeluC * a * a);
-  *da = dgel * (0.5f * (1.0f + p.t) + 0.5f * a * (1.0f - p.t * p.t) * dz);
+  *da = geglu_dgate(a, p.t, E::round(g * b));
 }
 
 }  // namespace gelu

@@ -70,6 +70,33 @@ struct GemmArgs {
   uint32_t spin_limit;
 };
 
+// Two 16-bit values in one 32-bit word (low half first): one cvt.rn.*x2 rounds a pair, and the
+// rounded values come back to fp32 with integer ops, so the epilogue's conversions take half the
+// conversion-pipe slots of per-element rounding, with the same round-to-nearest-even result.
+template <bool F16> struct Pair;
+template <> struct Pair<false> {
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) { return pack_bf16x2(lo, hi); }
+  static __device__ __forceinline__ float lo(uint32_t v) { return __uint_as_float(v << 16); }
+  static __device__ __forceinline__ float hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+};
+template <> struct Pair<true> {
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) { return pack_f16x2(lo, hi); }
+  static __device__ __forceinline__ float lo(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)v)); }
+  static __device__ __forceinline__ float hi(uint32_t v) {
+    return __half2float(__ushort_as_half((unsigned short)(v >> 16)));
+  }
+};
+
+// After an abort: wait (bounded) until the last kStages K blocks the producer issued have landed, so
+// no TMA load is still writing this CTA's shared memory when it exits.
+template <int S>
+__device__ __forceinline__ void drain_loads(uint64_t* full, int issued, uint32_t limit) {
+  for (int j = issued > S ? issued - S : 0; j < issued; ++j) {
+    for (uint32_t n = 0; n < limit && !mbar_try_wait(&full[j % S], (j / S) & 1); ++n) {
+    }
+  }
+}
+
 // K-major operand in the 128-byte swizzle: 8-row groups of 8 x 128 B (SBO = 1024 B); the K step of
 // 16 elements inside the swizzle row advances the start address by 32 B.
 __device__ __forceinline__ uint64_t kmajor_sw128(uint32_t addr) { return smem_desc(addr, 16, 1024, kSw128); }
@@ -80,8 +107,6 @@ linear_geglu_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                     const __grid_constant__ CUtensorMap ugmap, const __grid_constant__ CUtensorMap uvmap,
                     const __grid_constant__ CUtensorMap omap, const GemmArgs a) {
   pdl_enter();   // before any global access and before claiming TMEM
-  constexpr int DT = F16 ? KRSI_F16 : KRSI_BF16;
-  using E = Elem<DT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
@@ -152,7 +177,10 @@ linear_geglu_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
         __syncwarp();
       }
     }
-    if (!ok) watchdog_fire(kWdGemmLoad);
+    if (!ok) {
+      watchdog_fire(kWdGemmLoad);
+      drain_loads<kStages>(full, it, a.spin_limit);
+    }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (whole warp, elected lane)
     auto wait = [&](uint64_t* bar, uint32_t parity) {
@@ -197,7 +225,6 @@ linear_geglu_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
     }
   } else if (warp >= kEpiWarp0) {
     // ------------------------------------------------------------ epilogue
-    using T = typename E::T;
     const int ew = warp - kEpiWarp0;
     const int quarter = ew % 4;                 // TMEM lane quarter of this warp (warp % 4)
     const int half = ew / 4;                    // which 64 of the tile's 128 F-columns
@@ -230,23 +257,25 @@ linear_geglu_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[acc]);
         }
-        Vec16<T> ug[2], uv[2], o[2];
+        // per pair of columns: u rounded as the GEMM output, then gelu.cuh's geglu_out on the
+        // rounded values (gel rounded, times the value, rounded), pairs rounded together
+        using P = Pair<F16>;
+        uint32_t ug[kChunk / 2], uv[kChunk / 2], o[kChunk / 2];
 #pragma unroll
-        for (int e = 0; e < kChunk; ++e) {
-          const T ga = E::store(__uint_as_float(gv[e]));   // u, rounded as the GEMM output
-          const T vb = E::store(__uint_as_float(vv[e]));
-          ug[e / 8].v[e % 8] = ga;
-          uv[e / 8].v[e % 8] = vb;
-          o[e / 8].v[e % 8] = E::store(gelu::geglu_out<DT>(E::load(ga), E::load(vb)));
+        for (int e = 0; e < kChunk / 2; ++e) {
+          ug[e] = P::pack(__uint_as_float(gv[2 * e]), __uint_as_float(gv[2 * e + 1]));
+          uv[e] = P::pack(__uint_as_float(vv[2 * e]), __uint_as_float(vv[2 * e + 1]));
+          const uint32_t gel = P::pack(gelu::gelu_parts(P::lo(ug[e])).gel, gelu::gelu_parts(P::hi(ug[e])).gel);
+          o[e] = P::pack(P::lo(gel) * P::lo(uv[e]), P::hi(gel) * P::hi(uv[e]));
         }
         // the previous step's boxes must have been read by the TMA unit before they are rewritten
         if (lane == 0) bulk_wait_read_all();
         __syncwarp();
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
-          *slot(0, p) = *reinterpret_cast<const uint4*>(&ug[p]);
-          *slot(1, p) = *reinterpret_cast<const uint4*>(&uv[p]);
-          *slot(2, p) = *reinterpret_cast<const uint4*>(&o[p]);
+          *slot(0, p) = make_uint4(ug[4 * p], ug[4 * p + 1], ug[4 * p + 2], ug[4 * p + 3]);
+          *slot(1, p) = make_uint4(uv[4 * p], uv[4 * p + 1], uv[4 * p + 2], uv[4 * p + 3]);
+          *slot(2, p) = make_uint4(o[4 * p], o[4 * p + 1], o[4 * p + 2], o[4 * p + 3]);
         }
         fence_async_shared();                      // staged boxes -> visible to the TMA unit
         __syncwarp();
@@ -269,23 +298,300 @@ linear_geglu_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
-// 2-D view (cols, rows) of a row-major 16-bit matrix with `pitch` elements between rows.  Loads
-// (box 64 x 128, 128-byte swizzle) read elements past cols or rows as zero; stores (box 16 x 32,
-// 32-byte swizzle) skip them.
+// ---------------------------------------------------------------- backward: du = geglu_bwd(dy @ w, u)
+// The down projection's input gradient g = dy @ w (dy [rows, K], w [K, F]: the down projection's
+// nn.Linear weight, read MN-major) with GEGLU's backward in the epilogue: g never goes to memory.
+// Tiles of 128 rows x 256 F-columns; per K block the dy tile [128 x 64] (K-major) and four w boxes
+// [64 K-rows x 64 columns] (MN-major), 48 KB per stage.  Each epilogue warp owns 32 rows x 128
+// columns, 16 at a time: its u-gate and u-value boxes arrive by TMA (the next step's are requested as
+// soon as the current ones are in registers), g comes from TMEM rounded as the GEMM output, and
+// du-gate, du-value leave through staged boxes and TMA stores.
+// The u boxes come from HBM (u was written a whole forward ago), about a microsecond away, and a step
+// takes less: each warp keeps a ring of three u slots with the next two steps' loads in flight.  The
+// ring's 48 KB come out of the operand ring, which has three stages here (measured with one u slot:
+// every step waited for its own load, 449 us per call at the block's shape).
+constexpr int kBwdBN = 256;                                   // F-columns per tile (UMMA N)
+constexpr int kBwdStages = 3;
+constexpr int kUSlots = 3;                                    // u boxes per epilogue warp: 2 loads ahead
+constexpr uint32_t kBwdWBox = 64 * kBK * 2;                   // one [64 K-rows x 64 columns] w box: 8 KB
+constexpr uint32_t kBwdStageBytes = kATile + 4 * kBwdWBox;
+constexpr uint32_t kBwdIoBytes = (2 * kUSlots + 2) * kBoxBytes;   // per epilogue warp: u slots, du gate, du value
+constexpr uint32_t kBwdIoOff = kBwdStages * kBwdStageBytes;
+constexpr uint32_t kBwdBarOff = kBwdIoOff + kEpiWarps * kBwdIoBytes;
+// full[S], empty[S], acc_full[2], acc_empty[2], drain, u_full[epilogue warps][slots]
+constexpr int kBwdNumBars = 2 * kBwdStages + 2 + 2 + 1 + kEpiWarps * kUSlots;
+constexpr uint32_t kBwdMiscOff = kBwdBarOff + kBwdNumBars * 8;
+constexpr uint32_t kBwdSmem = kBwdMiscOff + 16 + 1024;
+static_assert(kBwdSmem <= 232448, "shared memory budget");
+
+// MN-major operand in the 128-byte swizzle: 64-column atoms of 8 K-rows x 128 B (SBO = 1024 B), the
+// next 64 columns one box further (LBO = 8 KB); the K step of 16 rows advances the start by 2 KB.
+__device__ __forceinline__ uint64_t mnmajor_sw128(uint32_t addr) { return smem_desc(addr, kBwdWBox, 1024, kSw128); }
+
+template <bool F16>
+__global__ void __launch_bounds__(kThreads, 1)
+linear_geglu_bwd_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_constant__ CUtensorMap wmap,
+                        const __grid_constant__ CUtensorMap ugmap, const __grid_constant__ CUtensorMap uvmap,
+                        const __grid_constant__ CUtensorMap dugmap, const __grid_constant__ CUtensorMap duvmap,
+                        const GemmArgs a) {
+  pdl_enter();   // before any global access and before claiming TMEM
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBwdBarOff);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kBwdStages;
+  uint64_t* acc_full = bars + 2 * kBwdStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint64_t* u_full = drain + 1;   // [epilogue warp][slot]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kBwdMiscOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kBwdMiscOff + 4);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int my_tiles = (int)blockIdx.x < a.n_tiles ? (a.n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  auto tile_of = [&](int i) { return (int)blockIdx.x + i * (int)gridDim.x; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kBwdStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kEpiWarps);
+    }
+    mbar_init(drain, 1);
+    for (int w = 0; w < kEpiWarps * kUSlots; ++w) mbar_init(&u_full[w], 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&dymap);
+    prefetch_tensormap(&wmap);
+  }
+  if (warp == kEpiWarp0 && lane == 0) {
+    prefetch_tensormap(&ugmap);
+    prefetch_tensormap(&uvmap);
+    prefetch_tensormap(&dugmap);
+    prefetch_tensormap(&duvmap);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    bool ok = true;
+    int it = 0;
+    for (int i = 0; i < my_tiles && ok; ++i) {
+      const int t = tile_of(i);
+      const int m0 = (t / a.n_ftiles) * kBM, n0 = (t % a.n_ftiles) * kBwdBN;
+      for (int kb = 0; kb < a.n_kb; ++kb, ++it) {
+        const int s = it % kBwdStages;
+        if (it >= kBwdStages && !__all_sync(0xffffffffu, mbar_wait_bounded(&empty[s], ((it / kBwdStages) - 1) & 1,
+                                                                            abort_flag, a.spin_limit))) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          uint8_t* st = smem + s * kBwdStageBytes;
+          mbar_arrive_expect_tx(&full[s], kBwdStageBytes);
+          tma_load_2d(st, &dymap, &full[s], kb * kBK, m0);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)   // w rows (K) kb*64.., columns n0 + 64 j..
+            tma_load_2d(st + kATile + j * kBwdWBox, &wmap, &full[s], n0 + 64 * j, kb * kBK);
+        }
+        __syncwarp();
+      }
+    }
+    if (!ok) {
+      watchdog_fire(kWdGemmLoad);
+      drain_loads<kBwdStages>(full, it, a.spin_limit);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, abort_flag, a.spin_limit));
+    };
+    constexpr uint32_t idesc = idesc_f16(kBM, kBwdBN, F16 ? 0u : 1u, false, true);   // w MN-major
+    const uint64_t adesc0 = kmajor_sw128(smem_u32(smem));
+    const uint64_t bdesc0 = mnmajor_sw128(smem_u32(smem + kATile));
+    constexpr uint64_t kStageStep = kBwdStageBytes >> 4;
+    constexpr uint64_t kAKStep = 32 >> 4;             // 16 K-columns of 2 bytes
+    constexpr uint64_t kBKStep = (16 * 128) >> 4;     // 16 K-rows of 128 bytes
+    bool ok = true;
+    int it = 0;
+    for (int i = 0; i < my_tiles && ok; ++i) {
+      const int acc = i & 1;
+      if (i >= 2 && !wait(&acc_empty[acc], ((i >> 1) - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d = tmem + acc * kBwdBN;
+      for (int kb = 0; kb < a.n_kb; ++kb, ++it) {
+        const int s = it % kBwdStages;
+        if (!wait(&full[s], (it / kBwdStages) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t ad = adesc0 + (uint64_t)s * kStageStep;
+        const uint64_t bd = bdesc0 + (uint64_t)s * kStageStep;
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk)
+          mma_ss_e(d, ad + kk * kAKStep, bd + kk * kBKStep, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+        mma_commit_e(&empty[s]);
+      }
+      if (!ok) break;
+      mma_commit_e(&acc_full[acc]);
+    }
+    if (!ok && my_tiles > 0) watchdog_fire(kWdGemmMma);
+    mma_commit_e(drain);
+    for (uint32_t i = 0; i < a.spin_limit && !mbar_try_wait(drain, 0); ++i) {
+    }
+  } else if (warp >= kEpiWarp0) {
+    // ------------------------------------------------------------ epilogue
+    using P = Pair<F16>;
+    constexpr int kSteps = 128 / kChunk;        // 16-column steps per warp per tile
+    const int ew = warp - kEpiWarp0;
+    const int quarter = ew % 4;
+    const int half = ew / 4;                    // which 128 of the tile's 256 F-columns
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    uint8_t* io = smem + kBwdIoOff + ew * kBwdIoBytes;   // [slot][u gate | u value], then du gate, du value
+    uint8_t* du_boxes = io + 2 * kUSlots * kBoxBytes;
+    uint64_t* ubar = &u_full[ew * kUSlots];
+    const int n_steps = my_tiles * kSteps;
+    auto slot = [&](uint8_t* box, int p) {
+      return reinterpret_cast<uint4*>(box + lane * 32 + ((p ^ ((lane >> 2) & 1)) << 4));
+    };
+    auto row0_of = [&](int i) { return (tile_of(i) / a.n_ftiles) * kBM + quarter * 32; };
+    auto col_of = [&](int i, int c) { return (tile_of(i) % a.n_ftiles) * kBwdBN + half * 128 + c * kChunk; };
+    // step q's u boxes (gate and value columns of this warp's rows; zero past rows or F) into slot q % 3
+    auto load_u = [&](int q) {
+      if (lane == 0) {
+        const int i = q / kSteps, c = q % kSteps, r = q % kUSlots;
+        uint8_t* box = io + r * 2 * kBoxBytes;
+        mbar_arrive_expect_tx(&ubar[r], 2 * kBoxBytes);
+        tma_load_2d(box, &ugmap, &ubar[r], col_of(i, c), row0_of(i));
+        tma_load_2d(box + kBoxBytes, &uvmap, &ubar[r], col_of(i, c), row0_of(i));
+      }
+    };
+    int issued = 0;             // u loads issued (steps 0 .. issued - 1)
+    for (; issued < kUSlots - 1 && issued < n_steps; ++issued) load_u(issued);
+    bool ok = true;
+    int q = 0;                  // steps whose u has arrived
+    for (int i = 0; i < my_tiles && ok; ++i) {
+      const int acc = i & 1;
+      const int row0 = row0_of(i);
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&acc_full[acc], (i >> 1) & 1, abort_flag, a.spin_limit))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t acc_addr = tmem + lane_addr + acc * kBwdBN + half * 128;
+#pragma unroll 1
+      for (int c = 0; c < kSteps; ++c) {
+        uint32_t gv[kChunk];
+        tmem_ld16(acc_addr + c * kChunk, gv);
+        tmem_wait_ld();
+        if (c + 1 == kSteps) {                  // the accumulator has been read: the MMA may reuse it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        }
+        const int r = q % kUSlots;
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&ubar[r], (q / kUSlots) & 1, abort_flag, a.spin_limit))) {
+          ok = false;
+          break;
+        }
+        ++q;
+        uint8_t* ubox = io + r * 2 * kBoxBytes;
+        uint4 av[2], bv[2];
+#pragma unroll
+        for (int p2 = 0; p2 < 2; ++p2) {
+          av[p2] = *slot(ubox, p2);
+          bv[p2] = *slot(ubox + kBoxBytes, p2);
+        }
+        __syncwarp();                           // every lane has its u: slot r may be refilled
+        if (issued < n_steps) load_u(issued++); // two steps ahead, into the slot read one step ago
+        const uint32_t aw[8] = {av[0].x, av[0].y, av[0].z, av[0].w, av[1].x, av[1].y, av[1].z, av[1].w};
+        const uint32_t bw[8] = {bv[0].x, bv[0].y, bv[0].z, bv[0].w, bv[1].x, bv[1].y, bv[1].z, bv[1].w};
+        // per pair of columns: g rounded as the GEMM output, then gelu.cuh's geglu_grad arithmetic
+        uint32_t dg[kChunk / 2], dv[kChunk / 2];
+#pragma unroll
+        for (int e = 0; e < kChunk / 2; ++e) {
+          const uint32_t g2 = P::pack(__uint_as_float(gv[2 * e]), __uint_as_float(gv[2 * e + 1]));
+          const float a0 = P::lo(aw[e]), a1 = P::hi(aw[e]);
+          const gelu::GeluParts p0 = gelu::gelu_parts(a0), p1 = gelu::gelu_parts(a1);
+          const uint32_t gel = P::pack(p0.gel, p1.gel);
+          dv[e] = P::pack(P::lo(g2) * P::lo(gel), P::hi(g2) * P::hi(gel));             // db
+          const uint32_t dgel = P::pack(P::lo(g2) * P::lo(bw[e]), P::hi(g2) * P::hi(bw[e]));
+          dg[e] = P::pack(gelu::geglu_dgate(a0, p0.t, P::lo(dgel)), gelu::geglu_dgate(a1, p1.t, P::hi(dgel)));
+        }
+        if (lane == 0) bulk_wait_read_all();    // the previous step's du boxes have been read
+        __syncwarp();
+#pragma unroll
+        for (int p2 = 0; p2 < 2; ++p2) {
+          *slot(du_boxes, p2) = make_uint4(dg[4 * p2], dg[4 * p2 + 1], dg[4 * p2 + 2], dg[4 * p2 + 3]);
+          *slot(du_boxes + kBoxBytes, p2) = make_uint4(dv[4 * p2], dv[4 * p2 + 1], dv[4 * p2 + 2], dv[4 * p2 + 3]);
+        }
+        fence_async_shared();
+        __syncwarp();
+        const int col = col_of(i, c);
+        if (lane == 0 && col < a.F && row0 < a.rows) {
+          tma_store_2d(&dugmap, du_boxes, col, row0);
+          tma_store_2d(&duvmap, du_boxes + kBoxBytes, col, row0);
+          bulk_commit_group();
+        }
+      }
+    }
+    for (int j = q; j < issued; ++j)            // after an abort: the u loads in flight land first
+      for (uint32_t n = 0; n < a.spin_limit && !mbar_try_wait(&ubar[j % kUSlots], (j / kUSlots) & 1); ++n) {
+      }
+    if (lane == 0) bulk_wait_all();
+    if (!ok) watchdog_fire(kWdGemmEpilogue);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+// 2-D view (cols, rows) of a row-major 16-bit matrix with `pitch` elements between rows, copied in
+// boxes of box_cols x box_rows with the given swizzle.  Loads read elements past cols or rows as
+// zero; stores skip them.
 bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t pitch, bool f16,
-              bool store_box) {
+              uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
   attn::EncodeTiledFn enc = attn::encode_fn();
   if (!enc) return false;
   memset(map, 0, sizeof(*map));
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)pitch * 2};
-  cuuint32_t box[2] = {store_box ? (cuuint32_t)kChunk : (cuuint32_t)kBK, store_box ? 32u : (cuuint32_t)kBM};
+  cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   store_box ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+// The three box shapes: K-major operand tiles [128 rows x 64] (128-byte swizzle), MN-major weight tiles
+// [64 K-rows x 64 columns] (128-byte swizzle), and the epilogue's per-warp [32 rows x 16] boxes
+// (32-byte swizzle).
+bool operand_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, bool f16) {
+  return make_map(m, base, rows, cols, cols, f16, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+bool mn_operand_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, bool f16) {
+  return make_map(m, base, rows, cols, cols, f16, 64, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+bool box_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t pitch, bool f16) {
+  return make_map(m, base, rows, cols, pitch, f16, kChunk, 32, CU_TENSOR_MAP_SWIZZLE_32B);
 }
 
 template <bool F16>
@@ -295,6 +601,16 @@ int launch(const CUtensorMap& xm, const CUtensorMap& wm, const CUtensorMap& ugm,
   KRSI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
   const int grid = a.n_tiles < device_sm_count() ? a.n_tiles : device_sm_count();
   KRSI_CUDA_TRY(launch_pdl(kern, dim3(grid), dim3(kThreads), kSmem, stream, xm, wm, ugm, uvm, om, a));
+  return KRSI_OK;
+}
+
+template <bool F16>
+int launch_bwd(const CUtensorMap& dym, const CUtensorMap& wm, const CUtensorMap& ugm, const CUtensorMap& uvm,
+               const CUtensorMap& dugm, const CUtensorMap& duvm, const GemmArgs& a, cudaStream_t stream) {
+  auto kern = linear_geglu_bwd_kernel<F16>;
+  KRSI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBwdSmem));
+  const int grid = a.n_tiles < device_sm_count() ? a.n_tiles : device_sm_count();
+  KRSI_CUDA_TRY(launch_pdl(kern, dim3(grid), dim3(kThreads), kBwdSmem, stream, dym, wm, ugm, uvm, dugm, duvm, a));
   return KRSI_OK;
 }
 
@@ -316,14 +632,39 @@ extern "C" int krsi_linear_geglu_fwd(const void* x, const void* w, void* u, void
   const bool f16 = dtype == KRSI_F16;
   CUtensorMap xm, wm, ugm, uvm, om;
   const size_t esz = 2;
-  if (!make_map(&xm, x, rows, K, K, f16, false) || !make_map(&wm, w, 2 * F, K, K, f16, false) ||
-      !make_map(&ugm, u, rows, F, 2 * F, f16, true) ||
-      !make_map(&uvm, static_cast<const char*>(u) + F * esz, rows, F, 2 * F, f16, true) ||
-      !make_map(&om, out, rows, F, F, f16, true))
+  if (!operand_map(&xm, x, rows, K, f16) || !operand_map(&wm, w, 2 * F, K, f16) ||
+      !box_map(&ugm, u, rows, F, 2 * F, f16) || !box_map(&uvm, static_cast<const char*>(u) + F * esz, rows, F, 2 * F, f16) ||
+      !box_map(&om, out, rows, F, F, f16))
     return KRSI_ERR_CUDA;
   const int64_t n_rt = (rows + kBM - 1) / kBM, n_ft = (F + kBF - 1) / kBF;
   if (n_rt * n_ft > INT32_MAX) return KRSI_ERR_UNSUPPORTED;
   GemmArgs a{u, out, (int)rows, (int)K, (int)F, (int)n_ft, (int)(n_rt * n_ft), (int)((K + kBK - 1) / kBK),
              kSpinLimit};
   return f16 ? launch<true>(xm, wm, ugm, uvm, om, a, stream) : launch<false>(xm, wm, ugm, uvm, om, a, stream);
+}
+
+extern "C" int krsi_linear_geglu_bwd(const void* dy, const void* w, const void* u, void* du, int64_t rows,
+                                     int64_t K, int64_t F, int dtype, cudaStream_t stream) {
+  KRSI_CHECK_ARG(rows >= 0 && K > 0 && F > 0);
+  if (rows == 0) return KRSI_OK;
+  KRSI_CHECK_ARG(dy && w && u && du);
+  if (dtype != KRSI_BF16 && dtype != KRSI_F16) return KRSI_ERR_UNSUPPORTED;
+  // TMA: 16-byte aligned bases and row strides (K % 8 for dy, F % 8 for w, u and du)
+  if (K % 8 != 0 || F % 8 != 0) return KRSI_ERR_UNSUPPORTED;
+  if (!aligned16(dy) || !aligned16(w) || !aligned16(u) || !aligned16(du)) return KRSI_ERR_MISALIGNED;
+  if (rows > INT32_MAX - kBM || K > INT32_MAX - kBK || 2 * F > INT32_MAX - kBwdBN) return KRSI_ERR_UNSUPPORTED;
+  const bool f16 = dtype == KRSI_F16;
+  const size_t esz = 2;
+  CUtensorMap dym, wm, ugm, uvm, dugm, duvm;
+  if (!operand_map(&dym, dy, rows, K, f16) || !mn_operand_map(&wm, w, K, F, f16) ||
+      !box_map(&ugm, u, rows, F, 2 * F, f16) || !box_map(&uvm, static_cast<const char*>(u) + F * esz, rows, F, 2 * F, f16) ||
+      !box_map(&dugm, du, rows, F, 2 * F, f16) ||
+      !box_map(&duvm, static_cast<char*>(du) + F * esz, rows, F, 2 * F, f16))
+    return KRSI_ERR_CUDA;
+  const int64_t n_rt = (rows + kBM - 1) / kBM, n_ft = (F + kBwdBN - 1) / kBwdBN;
+  if (n_rt * n_ft > INT32_MAX) return KRSI_ERR_UNSUPPORTED;
+  GemmArgs a{nullptr, du, (int)rows, (int)K, (int)F, (int)n_ft, (int)(n_rt * n_ft), (int)((K + kBK - 1) / kBK),
+             kSpinLimit};
+  return f16 ? launch_bwd<true>(dym, wm, ugm, uvm, dugm, duvm, a, stream)
+             : launch_bwd<false>(dym, wm, ugm, uvm, dugm, duvm, a, stream);
 }

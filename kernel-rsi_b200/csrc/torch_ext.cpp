@@ -156,6 +156,27 @@ std::tuple<at::Tensor, at::Tensor> linear_geglu_fwd(const at::Tensor& x_in, cons
   return {u, out};
 }
 
+at::Tensor linear_geglu_bwd(const at::Tensor& dy_in, const at::Tensor& w_in, const at::Tensor& u_in) {
+  check_cuda(dy_in, "dy");
+  check_cuda(w_in, "w");
+  check_cuda(u_in, "u");
+  TORCH_CHECK(dy_in.dim() == 2 && w_in.dim() == 2 && u_in.dim() == 2, "linear_geglu_bwd: 2-D tensors expected");
+  TORCH_CHECK(w_in.size(0) == dy_in.size(1), "linear_geglu_bwd: w must be [", dy_in.size(1), ", F]");
+  TORCH_CHECK(u_in.size(0) == dy_in.size(0) && u_in.size(1) == 2 * w_in.size(1),
+              "linear_geglu_bwd: u must be [", dy_in.size(0), ", ", 2 * w_in.size(1), "]");
+  TORCH_CHECK(dy_in.scalar_type() == w_in.scalar_type() && u_in.scalar_type() == w_in.scalar_type(),
+              "linear_geglu_bwd: dy, w and u must have one dtype");
+  c10::cuda::CUDAGuard guard(dy_in.device());
+  auto dy = dy_in.contiguous();
+  auto w = w_in.contiguous();
+  auto u = u_in.contiguous();
+  auto du = at::empty_like(u);
+  check_rc(krsi_linear_geglu_bwd(dy.data_ptr(), w.data_ptr(), u.data_ptr(), du.data_ptr(), dy.size(0), dy.size(1),
+                                 w.size(1), krsi_dtype_of(dy), at::cuda::getCurrentCUDAStream()),
+           "krsi_linear_geglu_bwd");
+  return du;
+}
+
 // ---------------------------------------------------------------- relpos attention
 void check_attn_shapes(const at::Tensor& qkv, const at::Tensor& pd, int64_t B, int64_t S, int64_t H, int64_t D) {
   TORCH_CHECK(B >= 0 && S >= 0 && H > 0 && D > 0, "relpos_attention: bad B/S/H/D");
@@ -263,6 +284,7 @@ TORCH_LIBRARY(krsi, m) {
   m.def("geglu_fwd(Tensor u) -> Tensor");
   m.def("geglu_bwd(Tensor g, Tensor u) -> Tensor");
   m.def("linear_geglu_fwd(Tensor x2d, Tensor w) -> (Tensor, Tensor)");
+  m.def("linear_geglu_bwd(Tensor dy, Tensor w, Tensor u) -> Tensor");
   m.def("relpos_attn_fwd(Tensor qkv, Tensor pd, int B, int S, int H, int D, float scale) -> (Tensor, Tensor, Tensor)");
   m.def("relpos_attn_bwd(Tensor dout, Tensor qkv, Tensor pd, Tensor out32, Tensor lse, int B, int S, int H, int D, "
         "float scale) -> (Tensor, Tensor)");
@@ -277,6 +299,7 @@ TORCH_LIBRARY_IMPL(krsi, CUDA, m) {
   m.impl("geglu_fwd", &geglu_fwd);
   m.impl("geglu_bwd", &geglu_bwd);
   m.impl("linear_geglu_fwd", &linear_geglu_fwd);
+  m.impl("linear_geglu_bwd", &linear_geglu_bwd);
   m.impl("relpos_attn_fwd", &relpos_attn_fwd);
   m.impl("relpos_attn_bwd", &relpos_attn_bwd);
   m.impl("t5_bias_fwd", &t5_bias_fwd);

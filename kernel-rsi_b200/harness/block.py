@@ -6,9 +6,12 @@ Each layer:  x -> RMSNorm -> fused q|k|v GEMM -> relpos attention (H heads of D)
 the four GEMMs are written straight into the all-reduce buckets when a LayerBucketAllReduce owns
 them)
 The attention, RMSNorm and GEGLU calls are the kernel-rsi library functions (relpos_attention(),
-rmsnorm(), geglu(), with the reference's signatures); the GEMMs are torch matmuls (cuBLAS).  loss =
-mean(out.float()^2).  Weights are bf16 ~ N(0, 0.02) (RMSNorm weights 1 + N(0, 0.02)), the per-layer
-relative-position table pd [H, 2L-1] is fp32 ~ N(0, 0.02).
+rmsnorm(), geglu(), with the reference's signatures); the GEMMs are torch matmuls (cuBLAS), except
+that on the B200 kernels the gate|value GEMM and the GEGLU forward are one tcgen05 kernel
+(krsi::linear_geglu_fwd, GEGLU in the GEMM's epilogue) and so are the down projection's input
+gradient and GEGLU's backward (krsi::linear_geglu_bwd).  loss = mean(out.float()^2).  Weights are
+bf16 ~ N(0, 0.02) (RMSNorm weights 1 + N(0, 0.02)), the per-layer relative-position table pd
+[H, 2L-1] is fp32 ~ N(0, 0.02).
 
 `ops` supplies the three library functions, so the same model runs on the B200 kernels or, for
 CPU tests of the distributed harness, on any stand-in with the same signatures.
@@ -62,14 +65,7 @@ class _Linear(torch.autograd.Function):
     def backward(ctx, g):
         x, w = ctx.saved_tensors
         gx = g @ w if ctx.needs_input_grad[0] else None
-        gw = None
-        if ctx.needs_input_grad[1]:
-            sink = grad_sink(ctx.w)
-            if sink is not None and ctx.w.grad is not None:
-                torch.mm(g.t(), x, out=ctx.w.grad)
-                sink.mark_ready(ctx.w)
-            else:
-                gw = g.t() @ x
+        gw = _weight_grad(ctx.w, g, x) if ctx.needs_input_grad[1] else None
         return gx, gw, (g if ctx.has_res else None)
 
 
@@ -118,6 +114,49 @@ class _RMSNormSkip(torch.autograd.Function):
         return dx, dw, None
 
 
+def _weight_grad(w, g, x):
+    """dW = g^T x: written straight into the weight's bucket view when a gradient all-reduce owns it
+    (and the bucket told it is ready), else returned for autograd to accumulate."""
+    sink = grad_sink(w)
+    if sink is not None and w.grad is not None:
+        torch.mm(g.t(), x, out=w.grad)
+        sink.mark_ready(w)
+        return None
+    return g.t() @ x
+
+
+class _FeedForward(torch.autograd.Function):
+    """res + geglu(x @ wi^T) @ wo^T on the two fused kernels: the gate|value projection with GEGLU in
+    its epilogue (krsi::linear_geglu_fwd, which also returns u) and, in the backward, the down
+    projection's input gradient with GEGLU's backward in its epilogue (krsi::linear_geglu_bwd), so
+    GEGLU's input gradient never reaches memory.  Weight gradients go into their buckets as in
+    _Linear."""
+
+    @staticmethod
+    def forward(ctx, x, wi, wo, res, ops):
+        u, g = ops.linear_geglu_fwd(x, wi)
+        ctx.save_for_backward(x, wi, wo, u, g)
+        ctx.wi, ctx.wo, ctx.ops = wi, wo, ops
+        return torch.addmm(res, g, wo.t())
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, wi, wo, u, g = ctx.saved_tensors
+        gy = gy.contiguous()
+        gwo = _weight_grad(ctx.wo, gy, g) if ctx.needs_input_grad[2] else None
+        du = ctx.ops.linear_geglu_bwd(gy, wo, u)
+        gx = du @ wi if ctx.needs_input_grad[0] else None
+        gwi = _weight_grad(ctx.wi, du, x) if ctx.needs_input_grad[1] else None
+        return gx, gwi, gwo, gy, None
+
+
+def _feed_forward(ops, h, wi, wo, res):
+    """res + geglu(h @ wi^T) @ wo^T: the fused kernels when `ops` runs on the B200 kernels."""
+    if getattr(ops, "fused_ffn", False):
+        return _FeedForward.apply(h, wi, wo, res, ops)
+    return _Linear.apply(ops.geglu(_Linear.apply(h, wi, None)), wo, res)
+
+
 def _norm_and_skip(ops, x2, w, eps):
     """The normalised rows and the residual input: fused when `ops` runs on the B200 kernels."""
     if getattr(ops, "fused_norm_skip", False):
@@ -159,12 +198,12 @@ class Layer(nn.Module):
             a = _Mark.apply(a, marks[1], marks[2])
         x2 = _Linear.apply(a, self.wo, x2)          # residual add inside the GEMM (beta = 1)
         h, x2 = _norm_and_skip(ops, x2, self.norm2, cfg.eps)
-        g = ops.geglu(_Linear.apply(h, self.wi, None))
-        x2 = _Linear.apply(g, self.wo2, x2)
+        x2 = _feed_forward(ops, h, self.wi, self.wo2, x2)
         return x2.reshape(B, L, d)
 
     def linear_weights(self):
-        """The weights used through _Linear (their gradients can be written into a bucket)."""
+        """The weights used through _Linear / _FeedForward (their gradients can be written into a
+        bucket)."""
         return [self.wqkv, self.wo, self.wi, self.wo2]
 
 
@@ -238,3 +277,9 @@ class LibraryOps:
         self.relpos_attention = relpos_attention.relpos_attention
         # RMSNorm and the residual branch share their input: one backward kernel adds both gradients
         self.fused_norm_skip = True
+        # the feed-forward on the fused kernels: the gate|value projection with GEGLU in its epilogue,
+        # the down projection's input gradient with GEGLU's backward in its epilogue
+        import linear_geglu  # noqa: F401  (loads the library's op registrations)
+        self.linear_geglu_fwd = torch.ops.krsi.linear_geglu_fwd
+        self.linear_geglu_bwd = torch.ops.krsi.linear_geglu_bwd
+        self.fused_ffn = True

@@ -101,6 +101,10 @@ def _register_compile_support() -> None:
     def _(x2d, w):
         return x2d.new_empty((x2d.shape[0], w.shape[0])), x2d.new_empty((x2d.shape[0], w.shape[0] // 2))
 
+    @reg_fake("krsi::linear_geglu_bwd")
+    def _(dy, w, u):
+        return torch.empty_like(u)
+
     @reg_fake("krsi::relpos_attn_fwd")
     def _(qkv, pd, B, S, H, D, scale):
         return (qkv.new_empty((B * S, H * D)), qkv.new_empty((B * S, H * D), dtype=torch.float32),

@@ -7,7 +7,8 @@ called as forward(mod, ...) with the original module's parameters).
   position bias     library t5_bias.t5_relpos_bias(): the bucket table -> per-distance bias row
   attention         library relpos_attention() with scale 1 (T5 folds the scale into its weights)
   o + residual      addmm (the residual rides in the GEMM)
-  wi_0 | wi_1 GEMM  one GEMM; library geglu() (gelu_tanh(gate) * value)
+  wi_0 | wi_1 GEMM  one tcgen05 GEMM with GEGLU (gelu_tanh(gate) * value) in its epilogue:
+                    library linear_geglu() (geglu() of the GEMM's output, bit for bit)
   wo + residual     addmm
 """
 import sys
@@ -18,7 +19,7 @@ import torch
 _LIB = Path(__file__).resolve().parent.parent / "library"
 if str(_LIB) not in sys.path:
     sys.path.insert(0, str(_LIB))
-import geglu  # noqa: E402
+import linear_geglu  # noqa: E402
 import relpos_attention  # noqa: E402
 import rmsnorm  # noqa: E402
 import t5_bias  # noqa: E402
@@ -36,6 +37,6 @@ def forward(mod, x):
     a = relpos_attention.relpos_attention(qkv, pd, B, S, H, D, 1.0)
     x2 = torch.addmm(x2, a, mod.o.weight.t())
     h = rmsnorm.rmsnorm(x2, mod.ln2.weight, mod.ln2.eps)
-    u = h @ torch.cat([mod.wi_0.weight, mod.wi_1.weight]).t()
-    x2 = torch.addmm(x2, geglu.geglu(u), mod.wo.weight.t())
+    g = linear_geglu.linear_geglu(h, torch.cat([mod.wi_0.weight, mod.wi_1.weight]))
+    x2 = torch.addmm(x2, g, mod.wo.weight.t())
     return x2.view(B, S, d)

@@ -35,3 +35,13 @@ def test_oracle_only_in_the_cpu_baseline_leg():
     for node in ast.walk(tree):
         if isinstance(node, ast.FunctionDef) and imports_oracle(node):
             assert node.name in allowed, node.name
+
+
+def test_reference_arm_linear_geglu_line():
+    """The fused projection + GEGLU workload's reference arm: the reference torch path on a row
+    sample, in the fused kernel's metric (TFLOP/s)."""
+    p = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--workload", "linear_geglu",
+                        "--steps", "1", "--warmup", "3"], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert p.returncode == 0, p.stderr[-2000:]
+    d = json.loads([l for l in p.stdout.splitlines() if l.startswith("{")][-1])
+    assert d["impl"] == "reference" and d["unit"] == "TFLOP/s" and d["value"] > 0

@@ -178,3 +178,24 @@ def test_two_gpu_allreduced_gradients_equal_full_batch():
         for which in (3, 4):                 # eager and graphed steps
             for g, gref in zip(res[r][which], ref):
                 assert norm_max_err(torch.from_numpy(g), gref) <= 1e-2
+
+
+def test_fused_ffn_matches_the_unfused_block():
+    """The block with the gate|value GEMM and GEGLU as one kernel (krsi::linear_geglu_fwd) against the
+    same block with cuBLAS's GEMM followed by the GEGLU kernel: the fused kernel rounds u once from an
+    fp32 accumulator as cuBLAS does and applies the GEGLU kernel's arithmetic to it, so the loss, the
+    output and every gradient agree to the accumulation order of the two GEMMs.  The forward is
+    deterministic (output and loss to 1e-3); the gradients also carry the attention backward's
+    run-to-run dQ accumulation order (its TMA reduce-adds land in any order), so they are held to
+    the block's 1e-2."""
+    ops = LibraryOps()
+    model = BlockStack(CFG, ops, dev, seed=3)
+    unfused_ops = LibraryOps()
+    unfused_ops.fused_ffn = False
+    x = batch(2).to(dev)
+    fused, names = fwd_bwd(model, x)
+    unfused, _ = fwd_bwd(with_ops(model, unfused_ops), x)
+    labels = ["out", "loss"] + names
+    errs = {k: norm_max_err(a.float(), b.float()) for k, a, b in zip(labels, fused, unfused)}
+    bad = {k: e for k, e in errs.items() if not e <= (1e-3 if k in ("out", "loss") else 1e-2)}
+    assert not bad, bad

@@ -88,3 +88,15 @@ def test_linear_geglu_argument_checks(lib):
     assert call(vp(16), vp(16), vp(16), vp(16), i64(4), i64(64), i64(20), 1, vp(0)) == 2
     assert call(vp(18), vp(16), vp(16), vp(16), i64(4), i64(64), i64(64), 1, vp(0)) == 3
     assert call(vp(0), vp(0), vp(0), vp(0), i64(0), i64(64), i64(64), 1, vp(0)) == 0
+
+
+def test_linear_geglu_bwd_argument_checks(lib):
+    """The fused down-projection input gradient + GEGLU backward refuses bad arguments before any
+    device work, like the forward."""
+    vp, i64 = ctypes.c_void_p, ctypes.c_int64
+    call = lib.krsi_linear_geglu_bwd
+    assert call(vp(16), vp(0), vp(16), vp(16), i64(4), i64(64), i64(64), 1, vp(0)) == 1
+    assert call(vp(16), vp(16), vp(16), vp(16), i64(4), i64(64), i64(64), 0, vp(0)) == 2
+    assert call(vp(16), vp(16), vp(16), vp(16), i64(4), i64(12), i64(64), 1, vp(0)) == 2
+    assert call(vp(16), vp(16), vp(24), vp(16), i64(4), i64(64), i64(64), 1, vp(0)) == 3
+    assert call(vp(0), vp(0), vp(0), vp(0), i64(0), i64(64), i64(64), 1, vp(0)) == 0

@@ -118,3 +118,89 @@ def test_c_abi_direct_call_and_errors():
     assert lib.krsi_linear_geglu_fwd(ptr(x), ptr(w), ptr(u), ptr(out), ctypes.c_int64(64), ctypes.c_int64(256),
                                      ctypes.c_int64(128), DT[torch.float32], stream()) == 2
     assert lib.krsi_linear_geglu_fwd(ctypes.c_void_p(x.data_ptr() + 2), ptr(w), ptr(u), ptr(out), *args) == 3
+
+
+# ---------------------------------------------------------------- backward: du = geglu_bwd(dy @ w, u)
+
+@pytest.mark.parametrize("rows,K,F,dt", [
+    (2048, 1152, 4608, torch.bfloat16),   # the block's down projection: dy [rows, 1152], wo [1152, 4608]
+    (300, 1152, 4608, torch.bfloat16),    # ragged last row tile
+    (1, 64, 8, torch.bfloat16),
+    (129, 72, 200, torch.bfloat16),       # K not a multiple of 64, F not a multiple of 256
+    (257, 1000, 136, torch.bfloat16),
+    (512, 768, 2048, torch.float16),      # T5 v1.1 base, f16
+])
+def test_bwd_fused_vs_oracle_and_standalone_geglu(rows, K, F, dt):
+    seed = rows + K + F
+    dy = O.gen((rows, K), seed).to(dt)
+    w = O.gen((K, F), seed + 1, std=K ** -0.5).to(dt)
+    u = O.gen((rows, 2 * F), seed + 2).to(dt)
+    du = torch.ops.krsi.linear_geglu_bwd(dy.to(dev), w.to(dev), u.to(dev))
+    # the unfused pair: cuBLAS's dy @ w (rounded once from fp32, as the fused kernel rounds g), then the
+    # GEGLU backward kernel: identical wherever the two GEMMs round g alike
+    du_pair = torch.ops.krsi.geglu_bwd(dy.to(dev) @ w.to(dev), u.to(dev))
+    assert (du == du_pair).float().mean().item() >= 0.999
+    g64 = (dy.double() @ w.double()).to(dt)
+    assert norm_max_err(du.cpu(), O.geglu_bwd(g64, u)) <= 1e-2
+    import _ext
+    assert _ext.device_status() == 0
+
+
+def ffn_inputs(rows, d, F, seed):
+    x = O.gen((rows, d), seed).to(torch.bfloat16)
+    wi = O.gen((2 * F, d), seed + 1, std=d ** -0.5).to(torch.bfloat16)
+    wo = O.gen((d, F), seed + 2, std=F ** -0.5).to(torch.bfloat16)
+    res = O.gen((rows, d), seed + 3).to(torch.bfloat16)
+    gy = O.gen((rows, d), seed + 4).to(torch.bfloat16)
+    return x, wi, wo, res, gy
+
+
+def test_feed_forward_autograd_vs_oracle_and_unfused():
+    """feed_forward (both fused kernels) against the fp64 oracle chain and against the library's
+    unfused composition (linear_geglu forward, GEGLU's backward kernel, cuBLAS GEMMs)."""
+    rows, d, F = 512, 1152, 4608
+    x, wi, wo, res, gy = ffn_inputs(rows, d, F, seed=6)
+    args = [t.to(dev).requires_grad_(True) for t in (x, wi, wo, res)]
+    y = krsi().feed_forward(*args)
+    grads = torch.autograd.grad(y, args, gy.to(dev))
+    args2 = [t.to(dev).requires_grad_(True) for t in (x, wi, wo, res)]
+    y2 = torch.addmm(args2[3], krsi().linear_geglu(args2[0], args2[1]), args2[2].t())
+    grads2 = torch.autograd.grad(y2, args2, gy.to(dev))
+    assert torch.equal(y, y2)
+    for a_, b_ in zip(grads, grads2):
+        assert norm_max_err(a_.float(), b_.float()) <= 1e-2
+    # fp64 oracle chain on the kernel's own u
+    u, g = torch.ops.krsi.linear_geglu_fwd(x.to(dev), wi.to(dev))
+    u, g = u.cpu(), g.cpu()
+    dg = (gy.double() @ wo.double()).to(torch.bfloat16)
+    dx_o, dwi_o = O.linear_geglu_bwd(dg, x, wi, u)
+    dwo_o = gy.double().t() @ g.double()
+    assert norm_max_err(grads[0].cpu(), dx_o) <= 1e-2
+    assert norm_max_err(grads[1].cpu(), dwi_o) <= 1e-2
+    assert norm_max_err(grads[2].cpu(), dwo_o) <= 1e-2
+    assert torch.equal(grads[3], gy.to(dev))
+
+
+def test_feed_forward_reference_criterion_bf16():
+    """The reference's selftest criterion on the whole feed-forward (T5 v1.1 base shape)."""
+    rows, d, F = 2048, 768, 2048
+    x, wi, wo, _, _ = ffn_inputs(rows, d, F, seed=8)
+    cot = O.gen((rows, d), 13).to(dev) * 1e-2
+    res, _, _ = reference_compare(krsi().feed_forward, krsi().feed_forward_reference,
+                                  [x.to(dev), wi.to(dev), wo.to(dev)], cot)
+    assert res["pass"], res
+
+
+def test_bwd_c_abi_and_errors():
+    lib = capi()
+    dy = O.gen((64, 256), 1).to(dev, torch.bfloat16)
+    w = O.gen((256, 128), 2).to(dev, torch.bfloat16)
+    u = O.gen((64, 256), 3).to(dev, torch.bfloat16)
+    du = torch.empty_like(u)
+    args = (ctypes.c_int64(64), ctypes.c_int64(256), ctypes.c_int64(128), DT[torch.bfloat16], stream())
+    assert lib.krsi_linear_geglu_bwd(ptr(dy), ptr(w), ptr(u), ptr(du), *args) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(du, torch.ops.krsi.linear_geglu_bwd(dy, w, u))
+    assert lib.krsi_linear_geglu_bwd(ptr(dy), ptr(w), ptr(u), ptr(du), ctypes.c_int64(64), ctypes.c_int64(250),
+                                     ctypes.c_int64(128), DT[torch.bfloat16], stream()) == 2
+    assert lib.krsi_linear_geglu_bwd(ptr(dy), ctypes.c_void_p(w.data_ptr() + 8), ptr(u), ptr(du), *args) == 3
