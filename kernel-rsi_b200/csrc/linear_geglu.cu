@@ -86,6 +86,15 @@ template <> struct Pair<true> {
     return __half2float(__ushort_as_half((unsigned short)(v >> 16)));
   }
 };
+// A rounded 16-bit pair as two fp32 lanes of one f32x2 register, and back (rounding both lanes).
+template <bool F16>
+__device__ __forceinline__ uint64_t widen(uint32_t v) { return f2_pack(Pair<F16>::lo(v), Pair<F16>::hi(v)); }
+template <bool F16>
+__device__ __forceinline__ uint32_t narrow(uint64_t v) {
+  float lo, hi;
+  f2_unpack(v, lo, hi);
+  return Pair<F16>::pack(lo, hi);
+}
 
 // After an abort: wait (bounded) until the last kStages K blocks the producer issued have landed, so
 // no TMA load is still writing this CTA's shared memory when it exits.
@@ -258,15 +267,15 @@ linear_geglu_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
           if (lane == 0) mbar_arrive(&acc_empty[acc]);
         }
         // per pair of columns: u rounded as the GEMM output, then gelu.cuh's geglu_out on the
-        // rounded values (gel rounded, times the value, rounded), pairs rounded together
+        // rounded values (gel rounded, times the value, rounded) in its paired form
         using P = Pair<F16>;
         uint32_t ug[kChunk / 2], uv[kChunk / 2], o[kChunk / 2];
 #pragma unroll
         for (int e = 0; e < kChunk / 2; ++e) {
           ug[e] = P::pack(__uint_as_float(gv[2 * e]), __uint_as_float(gv[2 * e + 1]));
           uv[e] = P::pack(__uint_as_float(vv[2 * e]), __uint_as_float(vv[2 * e + 1]));
-          const uint32_t gel = P::pack(gelu::gelu_parts(P::lo(ug[e])).gel, gelu::gelu_parts(P::hi(ug[e])).gel);
-          o[e] = P::pack(P::lo(gel) * P::lo(uv[e]), P::hi(gel) * P::hi(uv[e]));
+          const uint32_t gel = narrow<F16>(gelu::gelu_parts2(widen<F16>(ug[e])).gel);
+          o[e] = narrow<F16>(f2_mul(widen<F16>(gel), widen<F16>(uv[e])));
         }
         // the previous step's boxes must have been read by the TMA unit before they are rewritten
         if (lane == 0) bulk_wait_read_all();
@@ -522,17 +531,17 @@ linear_geglu_bwd_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_
         if (issued < n_steps) load_u(issued++); // two steps ahead, into the slot read one step ago
         const uint32_t aw[8] = {av[0].x, av[0].y, av[0].z, av[0].w, av[1].x, av[1].y, av[1].z, av[1].w};
         const uint32_t bw[8] = {bv[0].x, bv[0].y, bv[0].z, bv[0].w, bv[1].x, bv[1].y, bv[1].z, bv[1].w};
-        // per pair of columns: g rounded as the GEMM output, then gelu.cuh's geglu_grad arithmetic
+        // per pair of columns: g rounded as the GEMM output, then gelu.cuh's geglu_grad arithmetic in
+        // its paired form
         uint32_t dg[kChunk / 2], dv[kChunk / 2];
 #pragma unroll
         for (int e = 0; e < kChunk / 2; ++e) {
-          const uint32_t g2 = P::pack(__uint_as_float(gv[2 * e]), __uint_as_float(gv[2 * e + 1]));
-          const float a0 = P::lo(aw[e]), a1 = P::hi(aw[e]);
-          const gelu::GeluParts p0 = gelu::gelu_parts(a0), p1 = gelu::gelu_parts(a1);
-          const uint32_t gel = P::pack(p0.gel, p1.gel);
-          dv[e] = P::pack(P::lo(g2) * P::lo(gel), P::hi(g2) * P::hi(gel));             // db
-          const uint32_t dgel = P::pack(P::lo(g2) * P::lo(bw[e]), P::hi(g2) * P::hi(bw[e]));
-          dg[e] = P::pack(gelu::geglu_dgate(a0, p0.t, P::lo(dgel)), gelu::geglu_dgate(a1, p1.t, P::hi(dgel)));
+          const uint64_t g2 = widen<F16>(P::pack(__uint_as_float(gv[2 * e]), __uint_as_float(gv[2 * e + 1])));
+          const uint64_t a2 = widen<F16>(aw[e]);
+          const gelu::GeluParts2 pp = gelu::gelu_parts2(a2);
+          dv[e] = narrow<F16>(f2_mul(g2, widen<F16>(narrow<F16>(pp.gel))));                  // db
+          const uint64_t dgel = widen<F16>(narrow<F16>(f2_mul(g2, widen<F16>(bw[e]))));
+          dg[e] = narrow<F16>(gelu::geglu_dgate2(a2, pp.t, dgel));
         }
         if (lane == 0) bulk_wait_read_all();    // the previous step's du boxes have been read
         __syncwarp();
