@@ -14,6 +14,36 @@ namespace {
 using gelu::geglu_grad;
 using gelu::geglu_out;
 
+// A 16-byte packet of 16-bit elements as four pairs: gelu.cuh's paired forms (two lanes per f32x2
+// instruction, each pair rounded by one cvt.rn.*x2), the same bits as geglu_out / geglu_grad.
+template <int DT> struct Is16 { static constexpr bool value = DT != KRSI_F32; };
+
+template <int DT>
+__device__ __forceinline__ uint4 geglu_out_packet(uint4 a, uint4 b) {
+  constexpr bool F16 = DT == KRSI_F16;
+  auto one = [](uint32_t a2, uint32_t b2) {
+    const uint32_t gel = gelu::narrow<F16>(gelu::gelu_parts2(gelu::widen<F16>(a2)).gel);
+    return gelu::narrow<F16>(sm100::f2_mul(gelu::widen<F16>(gel), gelu::widen<F16>(b2)));
+  };
+  return make_uint4(one(a.x, b.x), one(a.y, b.y), one(a.z, b.z), one(a.w, b.w));
+}
+
+template <int DT>
+__device__ __forceinline__ void geglu_grad_packet(uint4 a, uint4 b, uint4 g, uint4* da, uint4* db) {
+  constexpr bool F16 = DT == KRSI_F16;
+  auto one = [](uint32_t a2, uint32_t b2, uint32_t g2w, uint32_t* da2, uint32_t* db2) {
+    const uint64_t g2 = gelu::widen<F16>(g2w), aa = gelu::widen<F16>(a2);
+    const gelu::GeluParts2 pp = gelu::gelu_parts2(aa);
+    *db2 = gelu::narrow<F16>(sm100::f2_mul(g2, gelu::widen<F16>(gelu::narrow<F16>(pp.gel))));
+    const uint64_t dgel = gelu::widen<F16>(gelu::narrow<F16>(sm100::f2_mul(g2, gelu::widen<F16>(b2))));
+    *da2 = gelu::narrow<F16>(gelu::geglu_dgate2(aa, pp.t, dgel));
+  };
+  one(a.x, b.x, g.x, &da->x, &db->x);
+  one(a.y, b.y, g.y, &da->y, &db->y);
+  one(a.z, b.z, g.z, &da->z, &db->z);
+  one(a.w, b.w, g.w, &da->w, &db->w);
+}
+
 // Vector path: items = rows * FV packets, FV = F / VEC.  Grid-stride over items, two
 // independent items per iteration so each thread keeps four 16-byte loads in flight.
 template <int DT>
@@ -36,14 +66,20 @@ geglu_fwd_vec(const typename Elem<DT>::T* __restrict__ u, typename Elem<DT>::T* 
     Vec16<T> a1, b1;
     if (has1) { a1 = ldg16_stream(u1); b1 = ldg16_stream(u1 + (size_t)FV * VEC); }
     Vec16<T> o0, o1;
+    if constexpr (Is16<DT>::value) {
+      auto u4 = [](const Vec16<T>& v) { return *reinterpret_cast<const uint4*>(&v); };
+      *reinterpret_cast<uint4*>(&o0) = geglu_out_packet<DT>(u4(a0), u4(b0));
+      if (has1) *reinterpret_cast<uint4*>(&o1) = geglu_out_packet<DT>(u4(a1), u4(b1));
+    } else {
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) o0.v[e] = E::store(geglu_out<DT>(E::load(a0.v[e]), E::load(b0.v[e])));
-    stg16(out + (size_t)i0 * VEC, o0);
-    if (has1) {
+      for (int e = 0; e < VEC; ++e) o0.v[e] = E::store(geglu_out<DT>(E::load(a0.v[e]), E::load(b0.v[e])));
+      if (has1) {
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) o1.v[e] = E::store(geglu_out<DT>(E::load(a1.v[e]), E::load(b1.v[e])));
-      stg16(out + (size_t)i1 * VEC, o1);
+        for (int e = 0; e < VEC; ++e) o1.v[e] = E::store(geglu_out<DT>(E::load(a1.v[e]), E::load(b1.v[e])));
+      }
     }
+    stg16(out + (size_t)i0 * VEC, o0);
+    if (has1) stg16(out + (size_t)i1 * VEC, o1);
   }
 }
 
@@ -63,12 +99,17 @@ geglu_bwd_vec(const typename Elem<DT>::T* __restrict__ g, const typename Elem<DT
     const auto bv = ldg16_stream(u + ua + (size_t)FV * VEC);
     const auto gv = ldg16_stream(g + (size_t)i * VEC);
     Vec16<T> dav, dbv;
+    if constexpr (Is16<DT>::value) {
+      auto u4 = [](const Vec16<T>& v) { return *reinterpret_cast<const uint4*>(&v); };
+      geglu_grad_packet<DT>(u4(av), u4(bv), u4(gv), reinterpret_cast<uint4*>(&dav), reinterpret_cast<uint4*>(&dbv));
+    } else {
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) {
-      float da, db;
-      geglu_grad<DT>(E::load(av.v[e]), E::load(bv.v[e]), E::load(gv.v[e]), &da, &db);
-      dav.v[e] = E::store(da);
-      dbv.v[e] = E::store(db);
+      for (int e = 0; e < VEC; ++e) {
+        float da, db;
+        geglu_grad<DT>(E::load(av.v[e]), E::load(bv.v[e]), E::load(gv.v[e]), &da, &db);
+        dav.v[e] = E::store(da);
+        dbv.v[e] = E::store(db);
+      }
     }
     stg16(du + ua, dav);
     stg16(du + ua + (size_t)FV * VEC, dbv);

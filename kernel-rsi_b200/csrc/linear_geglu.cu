@@ -70,31 +70,9 @@ struct GemmArgs {
   uint32_t spin_limit;
 };
 
-// Two 16-bit values in one 32-bit word (low half first): one cvt.rn.*x2 rounds a pair, and the
-// rounded values come back to fp32 with integer ops, so the epilogue's conversions take half the
-// conversion-pipe slots of per-element rounding, with the same round-to-nearest-even result.
-template <bool F16> struct Pair;
-template <> struct Pair<false> {
-  static __device__ __forceinline__ uint32_t pack(float lo, float hi) { return pack_bf16x2(lo, hi); }
-  static __device__ __forceinline__ float lo(uint32_t v) { return __uint_as_float(v << 16); }
-  static __device__ __forceinline__ float hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
-};
-template <> struct Pair<true> {
-  static __device__ __forceinline__ uint32_t pack(float lo, float hi) { return pack_f16x2(lo, hi); }
-  static __device__ __forceinline__ float lo(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)v)); }
-  static __device__ __forceinline__ float hi(uint32_t v) {
-    return __half2float(__ushort_as_half((unsigned short)(v >> 16)));
-  }
-};
-// A rounded 16-bit pair as two fp32 lanes of one f32x2 register, and back (rounding both lanes).
-template <bool F16>
-__device__ __forceinline__ uint64_t widen(uint32_t v) { return f2_pack(Pair<F16>::lo(v), Pair<F16>::hi(v)); }
-template <bool F16>
-__device__ __forceinline__ uint32_t narrow(uint64_t v) {
-  float lo, hi;
-  f2_unpack(v, lo, hi);
-  return Pair<F16>::pack(lo, hi);
-}
+using gelu::Pair;
+using gelu::narrow;
+using gelu::widen;
 
 // After an abort: wait (bounded) until the last kStages K blocks the producer issued have landed, so
 // no TMA load is still writing this CTA's shared memory when it exits.
