@@ -942,6 +942,13 @@ def run_profile_case(which: str, n: int, S: int | None):
             x = gen((n, 1152), 21, torch.bfloat16).to(dev)
             w = gen((2 * 4608, 1152), 22, torch.bfloat16, std=0.02).to(dev)
             ops.linear_geglu_fwd(x, w)
+        elif which == "linear_geglu_bwd":
+            from harness.inputs import gen
+
+            dy = gen((n, 1152), 23, torch.bfloat16).to(dev)
+            w = gen((1152, 4608), 24, torch.bfloat16, std=0.02).to(dev)
+            u = gen((n, 2 * 4608), 25, torch.bfloat16).to(dev)
+            ops.linear_geglu_bwd(dy, w, u)
         elif which == "t5_bias":
             H, nb = 16, 32
             g = torch.Generator().manual_seed(0)
