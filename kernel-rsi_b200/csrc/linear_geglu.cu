@@ -88,6 +88,81 @@ __device__ __forceinline__ void drain_loads(uint64_t* full, int issued, uint32_t
 // 16 elements inside the swizzle row advances the start address by 32 B.
 __device__ __forceinline__ uint64_t kmajor_sw128(uint32_t addr) { return smem_desc(addr, 16, 1024, kSw128); }
 
+// The forward epilogue of one warp (warps kEpiWarp0.. of a CTA): for each of the CTA's tiles, wait for
+// its accumulator, read it out 16 columns at a time, hand the accumulator back (`release`), and write u
+// and out through staged boxes and TMA stores.  `row_of(i)` is the tile's first row handled by this
+// CTA, `col_of(i)` its first F-column.  Returns false after an abort.
+template <bool F16, typename RowOf, typename ColOf, typename Release>
+__device__ __forceinline__ bool fwd_epilogue(uint8_t* smem, uint32_t tmem, int warp, int lane, int my_tiles,
+                                             uint64_t* acc_full, volatile int* abort_flag, const CUtensorMap* ugmap,
+                                             const CUtensorMap* uvmap, const CUtensorMap* omap, const GemmArgs& a,
+                                             RowOf row_of, ColOf col_of, Release release) {
+  const int ew = warp - kEpiWarp0;
+  const int quarter = ew % 4;                 // TMEM lane quarter of this warp (warp % 4)
+  const int half = ew / 4;                    // which 64 of the tile's 128 F-columns
+  const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+  uint8_t* boxes = smem + kOutOff + ew * 3 * kBoxBytes;   // [u gate | u value | out], 32-byte rows
+  // this lane's row, 16-byte packet p of a box in the 32-byte swizzle (chunk bit ^= row bit 2)
+  auto slot = [&](int box, int p) {
+    return reinterpret_cast<uint4*>(boxes + box * kBoxBytes + lane * 32 + ((p ^ ((lane >> 2) & 1)) << 4));
+  };
+  bool ok = true;
+  for (int i = 0; i < my_tiles; ++i) {
+    const int acc = i & 1;
+    const int row0 = row_of(i) + quarter * 32;   // this warp's first row
+    const int c_base = col_of(i) + half * 64;    // first F-column of this warp's 64
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&acc_full[acc], (i >> 1) & 1, abort_flag, a.spin_limit))) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    const uint32_t acc_addr = tmem + lane_addr + acc * kBN + half * 64;
+#pragma unroll 1
+    for (int c0 = 0; c0 < 64; c0 += kChunk) {
+      uint32_t gv[kChunk], vv[kChunk];
+      tmem_ld16(acc_addr + c0, gv);              // gate columns
+      tmem_ld16(acc_addr + kBF + c0, vv);        // value columns
+      tmem_wait_ld();
+      if (c0 + kChunk == 64) {                   // the accumulator has been read: the MMA may reuse it
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) release(acc);
+      }
+      // per pair of columns: u rounded as the GEMM output, then gelu.cuh's geglu_out on the
+      // rounded values (gel rounded, times the value, rounded) in its paired form
+      using P = Pair<F16>;
+      uint32_t ug[kChunk / 2], uv[kChunk / 2], o[kChunk / 2];
+#pragma unroll
+      for (int e = 0; e < kChunk / 2; ++e) {
+        ug[e] = P::pack(__uint_as_float(gv[2 * e]), __uint_as_float(gv[2 * e + 1]));
+        uv[e] = P::pack(__uint_as_float(vv[2 * e]), __uint_as_float(vv[2 * e + 1]));
+        const uint32_t gel = narrow<F16>(gelu::gelu_parts2(widen<F16>(ug[e])).gel);
+        o[e] = narrow<F16>(f2_mul(widen<F16>(gel), widen<F16>(uv[e])));
+      }
+      // the previous step's boxes must have been read by the TMA unit before they are rewritten
+      if (lane == 0) bulk_wait_read_all();
+      __syncwarp();
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        *slot(0, p) = make_uint4(ug[4 * p], ug[4 * p + 1], ug[4 * p + 2], ug[4 * p + 3]);
+        *slot(1, p) = make_uint4(uv[4 * p], uv[4 * p + 1], uv[4 * p + 2], uv[4 * p + 3]);
+        *slot(2, p) = make_uint4(o[4 * p], o[4 * p + 1], o[4 * p + 2], o[4 * p + 3]);
+      }
+      fence_async_shared();                      // staged boxes -> visible to the TMA unit
+      __syncwarp();
+      const int col = c_base + c0;
+      if (lane == 0 && col < a.F && row0 < a.rows) {   // the maps clip rows >= rows and columns >= F
+        tma_store_2d(ugmap, boxes, col, row0);
+        tma_store_2d(uvmap, boxes + kBoxBytes, col, row0);
+        tma_store_2d(omap, boxes + 2 * kBoxBytes, col, row0);
+        bulk_commit_group();
+      }
+    }
+  }
+  if (lane == 0) bulk_wait_all();               // every store has completed before the CTA exits
+  return ok;
+}
+
 template <bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
 linear_geglu_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
@@ -212,70 +287,10 @@ linear_geglu_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
     }
   } else if (warp >= kEpiWarp0) {
     // ------------------------------------------------------------ epilogue
-    const int ew = warp - kEpiWarp0;
-    const int quarter = ew % 4;                 // TMEM lane quarter of this warp (warp % 4)
-    const int half = ew / 4;                    // which 64 of the tile's 128 F-columns
-    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    uint8_t* boxes = smem + kOutOff + ew * 3 * kBoxBytes;   // [u gate | u value | out], 32-byte rows
-    // this lane's row, 16-byte packet p of a box in the 32-byte swizzle (chunk bit ^= row bit 2)
-    auto slot = [&](int box, int p) {
-      return reinterpret_cast<uint4*>(boxes + box * kBoxBytes + lane * 32 + ((p ^ ((lane >> 2) & 1)) << 4));
-    };
-    bool ok = true;
-    for (int i = 0; i < my_tiles; ++i) {
-      const int t = tile_of(i);
-      const int acc = i & 1;
-      const int row0 = (t / a.n_ftiles) * kBM + quarter * 32;   // this warp's first row
-      const int c_base = (t % a.n_ftiles) * kBF + half * 64;    // first F-column of this warp's 64
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&acc_full[acc], (i >> 1) & 1, abort_flag, a.spin_limit))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t acc_addr = tmem + lane_addr + acc * kBN + half * 64;
-#pragma unroll 1
-      for (int c0 = 0; c0 < 64; c0 += kChunk) {
-        uint32_t gv[kChunk], vv[kChunk];
-        tmem_ld16(acc_addr + c0, gv);              // gate columns
-        tmem_ld16(acc_addr + kBF + c0, vv);        // value columns
-        tmem_wait_ld();
-        if (c0 + kChunk == 64) {                   // the accumulator has been read: the MMA may reuse it
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[acc]);
-        }
-        // per pair of columns: u rounded as the GEMM output, then gelu.cuh's geglu_out on the
-        // rounded values (gel rounded, times the value, rounded) in its paired form
-        using P = Pair<F16>;
-        uint32_t ug[kChunk / 2], uv[kChunk / 2], o[kChunk / 2];
-#pragma unroll
-        for (int e = 0; e < kChunk / 2; ++e) {
-          ug[e] = P::pack(__uint_as_float(gv[2 * e]), __uint_as_float(gv[2 * e + 1]));
-          uv[e] = P::pack(__uint_as_float(vv[2 * e]), __uint_as_float(vv[2 * e + 1]));
-          const uint32_t gel = narrow<F16>(gelu::gelu_parts2(widen<F16>(ug[e])).gel);
-          o[e] = narrow<F16>(f2_mul(widen<F16>(gel), widen<F16>(uv[e])));
-        }
-        // the previous step's boxes must have been read by the TMA unit before they are rewritten
-        if (lane == 0) bulk_wait_read_all();
-        __syncwarp();
-#pragma unroll
-        for (int p = 0; p < 2; ++p) {
-          *slot(0, p) = make_uint4(ug[4 * p], ug[4 * p + 1], ug[4 * p + 2], ug[4 * p + 3]);
-          *slot(1, p) = make_uint4(uv[4 * p], uv[4 * p + 1], uv[4 * p + 2], uv[4 * p + 3]);
-          *slot(2, p) = make_uint4(o[4 * p], o[4 * p + 1], o[4 * p + 2], o[4 * p + 3]);
-        }
-        fence_async_shared();                      // staged boxes -> visible to the TMA unit
-        __syncwarp();
-        const int col = c_base + c0;
-        if (lane == 0 && col < a.F && row0 < a.rows) {   // the maps clip rows >= rows and columns >= F
-          tma_store_2d(&ugmap, boxes, col, row0);
-          tma_store_2d(&uvmap, boxes + kBoxBytes, col, row0);
-          tma_store_2d(&omap, boxes + 2 * kBoxBytes, col, row0);
-          bulk_commit_group();
-        }
-      }
-    }
-    if (lane == 0) bulk_wait_all();               // every store has completed before the CTA exits
+    const bool ok = fwd_epilogue<F16>(
+        smem, tmem, warp, lane, my_tiles, acc_full, abort_flag, &ugmap, &uvmap, &omap, a,
+        [&](int i) { return (tile_of(i) / a.n_ftiles) * kBM; }, [&](int i) { return (tile_of(i) % a.n_ftiles) * kBF; },
+        [&](int acc) { mbar_arrive(&acc_empty[acc]); });
     if (!ok) watchdog_fire(kWdGemmEpilogue);
   }
 
@@ -283,6 +298,172 @@ linear_geglu_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+// ---------------------------------------------------------------- forward on CTA pairs (cta_group::2)
+// The same op on tiles of 256 rows x 128 F-columns shared by the two CTAs of a cluster: each CTA loads
+// its own 128 rows of x and half of the W tile (the even CTA the gate rows, the odd CTA the value
+// rows), 32 KB per K block instead of 48, and the even CTA issues M256 N256 K16 MMAs that read both
+// CTAs' shared memory and accumulate into both CTAs' TMEM (its 128 rows x [gate | value] each).  Both
+// CTAs' loads complete on the even CTA's stage barriers; the even CTA's MMA completions are signalled
+// to the barriers of both; both CTAs' epilogue warps hand the accumulator back to the even CTA.  Six
+// stages fit where four did, so more of the operand stream is in flight (the one-CTA kernel's MMA
+// warp waits for operands ~55% of each tile).
+constexpr int kPairStages = 6;
+constexpr uint32_t kPairStageBytes = kATile + kBTile;              // 128 rows of x + 128 rows of W
+constexpr uint32_t kPairOutOff = kPairStages * kPairStageBytes;
+static_assert(kPairOutOff == kOutOff, "the forward epilogue's boxes sit at the same offset");
+constexpr uint32_t kPairBarOff = kPairOutOff + kEpiWarps * 3 * kBoxBytes;
+// full[S] (used in the even CTA), empty[S], acc_full[2], acc_empty[2] (even CTA), drain (even CTA)
+constexpr int kPairNumBars = 2 * kPairStages + 2 + 2 + 1;
+constexpr uint32_t kPairMiscOff = kPairBarOff + kPairNumBars * 8;
+constexpr uint32_t kPairSmem = kPairMiscOff + 16 + 1024;
+static_assert(kPairSmem <= 232448, "shared memory budget");
+
+template <bool F16>
+__global__ void __launch_bounds__(kThreads, 1)
+linear_geglu_pair_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                         const __grid_constant__ CUtensorMap ugmap, const __grid_constant__ CUtensorMap uvmap,
+                         const __grid_constant__ CUtensorMap omap, const GemmArgs a) {
+  pdl_enter();   // before any global access and before claiming TMEM
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPairBarOff);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kPairStages;
+  uint64_t* acc_full = bars + 2 * kPairStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kPairMiscOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kPairMiscOff + 4);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const bool even = rank == 0;
+  const int pair = (int)blockIdx.x / 2, n_pairs = (int)gridDim.x / 2;
+  const int my_tiles = pair < a.n_tiles ? (a.n_tiles - 1 - pair) / n_pairs + 1 : 0;
+  auto tile_of = [&](int i) { return pair + i * n_pairs; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&full[s], 1);      // the even CTA's expect_tx arrival + both CTAs' TMA bytes
+      mbar_init(&empty[s], 1);     // the even CTA's tcgen05.commit
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);                // the even CTA's tcgen05.commit
+      mbar_init(&acc_empty[b], 2 * kEpiWarps);   // one arrival per epilogue warp of both CTAs
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&xmap);
+    prefetch_tensormap(&wmap);
+  }
+  if (warp == kEpiWarp0 && lane == 0) {
+    prefetch_tensormap(&ugmap);
+    prefetch_tensormap(&uvmap);
+    prefetch_tensormap(&omap);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();   // both CTAs' barriers initialised and TMEM allocated before either signals the other
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    bool ok = true;
+    int it = 0;
+    for (int i = 0; i < my_tiles && ok; ++i) {
+      const int t = tile_of(i);
+      const int m0 = (t / a.n_ftiles) * (2 * kBM) + (int)rank * kBM, n0 = (t % a.n_ftiles) * kBF;
+      const int wrow = even ? n0 : a.F + n0;   // the even CTA holds the gate rows, the odd the value rows
+      for (int kb = 0; kb < a.n_kb; ++kb, ++it) {
+        const int s = it % kPairStages;
+        if (it >= kPairStages && !__all_sync(0xffffffffu, mbar_wait_bounded(&empty[s], ((it / kPairStages) - 1) & 1,
+                                                                            abort_flag, a.spin_limit))) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          uint8_t* st = smem + s * kPairStageBytes;
+          const uint32_t bar = mapa_shared(&full[s], 0);
+          if (even) mbar_arrive_expect_tx(&full[s], 2 * kPairStageBytes);
+          tma_load_2d_pair(st, &xmap, bar, kb * kBK, m0);
+          tma_load_2d_pair(st + kATile, &wmap, bar, kb * kBK, wrow);
+        }
+        __syncwarp();
+      }
+    }
+    if (!ok) {
+      watchdog_fire(kWdGemmLoad);
+      if (even) drain_loads<kPairStages>(full, it, a.spin_limit);   // covers both CTAs' loads of each stage
+    }
+  } else if (warp == 1 && even) {
+    // ------------------------------------------------------------ MMA issuer (even CTA, elected lane)
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, abort_flag, a.spin_limit));
+    };
+    constexpr uint32_t idesc = idesc_f16(2 * kBM, kBN, F16 ? 0u : 1u, false, false);
+    const uint64_t desc0 = kmajor_sw128(smem_u32(smem));
+    constexpr uint64_t kStageStep = kPairStageBytes >> 4;
+    constexpr uint64_t kBStep = kATile >> 4;
+    constexpr uint64_t kKStep = 32 >> 4;
+    bool ok = true;
+    int it = 0;
+    for (int i = 0; i < my_tiles && ok; ++i) {
+      const int acc = i & 1;
+      if (i >= 2 && !wait(&acc_empty[acc], ((i >> 1) - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d = tmem + acc * kBN;
+      for (int kb = 0; kb < a.n_kb; ++kb, ++it) {
+        const int s = it % kPairStages;
+        if (!wait(&full[s], (it / kPairStages) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t ad = desc0 + (uint64_t)s * kStageStep;
+        const uint64_t bd = ad + kBStep;
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk)
+          mma_ss_pair_e(d, ad + kk * kKStep, bd + kk * kKStep, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+        mma_commit_pair_e(mapa_shared(&empty[s], 0));   // stage s free in both CTAs
+        mma_commit_pair_e(mapa_shared(&empty[s], 1));
+      }
+      if (!ok) break;
+      mma_commit_pair_e(mapa_shared(&acc_full[acc], 0));
+      mma_commit_pair_e(mapa_shared(&acc_full[acc], 1));
+    }
+    if (!ok && my_tiles > 0) watchdog_fire(kWdGemmMma);
+    mma_commit_pair_e(mapa_shared(drain, 0));
+    for (uint32_t i = 0; i < a.spin_limit && !mbar_try_wait(drain, 0); ++i) {
+    }
+  } else if (warp >= kEpiWarp0) {
+    // ------------------------------------------------------------ epilogue (both CTAs, own rows)
+    const bool ok = fwd_epilogue<F16>(
+        smem, tmem, warp, lane, my_tiles, acc_full, abort_flag, &ugmap, &uvmap, &omap, a,
+        [&](int i) { return (tile_of(i) / a.n_ftiles) * (2 * kBM) + (int)rank * kBM; },
+        [&](int i) { return (tile_of(i) % a.n_ftiles) * kBF; },
+        [&](int acc) {
+          if (even) mbar_arrive(&acc_empty[acc]);
+          else mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
+        });
+    if (!ok) watchdog_fire(kWdGemmEpilogue);
+  }
+
+  tc_fence_before();
+  cluster_sync();   // the even CTA's MMAs (which read this CTA's shared memory and TMEM) are done
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem, kTmemCols);
 }
 
 // ---------------------------------------------------------------- backward: du = geglu_bwd(dy @ w, u)
@@ -581,6 +762,61 @@ bool box_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64
   return make_map(m, base, rows, cols, pitch, f16, kChunk, 32, CU_TENSOR_MAP_SWIZZLE_32B);
 }
 
+// Clusters of two of the pair kernel that fit on the device at once (0: no pair launch possible), per
+// device, queried once.
+template <bool F16>
+int pair_clusters() {
+  static int cached[64];
+  static bool done[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (!done[dev]) {
+    auto kern = linear_geglu_pair_kernel<F16>;
+    int n = 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmem) == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * 74);
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = kPairSmem;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+    }
+    cudaGetLastError();   // a refused query leaves no sticky error behind
+    cached[dev] = n;
+    done[dev] = true;
+  }
+  return cached[dev];
+}
+
+template <bool F16>
+int launch_pair(const CUtensorMap& xm, const CUtensorMap& wm, const CUtensorMap& ugm, const CUtensorMap& uvm,
+                const CUtensorMap& om, const GemmArgs& a, int max_clusters, cudaStream_t stream) {
+  auto kern = linear_geglu_pair_kernel<F16>;
+  const int clusters = a.n_tiles < max_clusters ? a.n_tiles : max_clusters;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kPairSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  KRSI_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, xm, wm, ugm, uvm, om, a));
+  return KRSI_OK;
+}
+
 template <bool F16>
 int launch(const CUtensorMap& xm, const CUtensorMap& wm, const CUtensorMap& ugm, const CUtensorMap& uvm,
            const CUtensorMap& om, const GemmArgs& a, cudaStream_t stream) {
@@ -627,6 +863,14 @@ extern "C" int krsi_linear_geglu_fwd(const void* x, const void* w, void* u, void
   if (n_rt * n_ft > INT32_MAX) return KRSI_ERR_UNSUPPORTED;
   GemmArgs a{u, out, (int)rows, (int)K, (int)F, (int)n_ft, (int)(n_rt * n_ft), (int)((K + kBK - 1) / kBK),
              kSpinLimit};
+  // More than one row tile: CTA pairs (M = 256 tiles), when the device runs clusters of two of them.
+  const int clusters = rows > kBM ? (f16 ? pair_clusters<true>() : pair_clusters<false>()) : 0;
+  if (clusters > 0) {
+    GemmArgs pa = a;
+    pa.n_tiles = (int)(((rows + 2 * kBM - 1) / (2 * kBM)) * n_ft);
+    return f16 ? launch_pair<true>(xm, wm, ugm, uvm, om, pa, clusters, stream)
+               : launch_pair<false>(xm, wm, ugm, uvm, om, pa, clusters, stream);
+  }
   return f16 ? launch<true>(xm, wm, ugm, uvm, om, a, stream) : launch<false>(xm, wm, ugm, uvm, om, a, stream);
 }
 
