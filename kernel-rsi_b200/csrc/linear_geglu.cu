@@ -496,6 +496,118 @@ static_assert(kBwdSmem <= 232448, "shared memory budget");
 // next 64 columns one box further (LBO = 8 KB); the K step of 16 rows advances the start by 2 KB.
 __device__ __forceinline__ uint64_t mnmajor_sw128(uint32_t addr) { return smem_desc(addr, kBwdWBox, 1024, kSw128); }
 
+// The backward epilogue of one warp (warps kEpiWarp0.. of a CTA): for each of the CTA's tiles, read g
+// out of TMEM 16 columns at a time, hand the accumulator back (`release`), bring in the matching u
+// boxes through a ring of kUSlots (`io_base`: this CTA's per-warp boxes, `u_full`: their barriers),
+// and write du through staged boxes and TMA stores.  `row_of(i)` is the tile's first row handled by
+// this CTA, `col_base_of(i)` its first F-column.  Returns false after an abort.
+template <bool F16, typename RowOf, typename ColOf, typename Release>
+__device__ __forceinline__ bool bwd_epilogue(uint8_t* io_base, uint64_t* u_full, uint32_t tmem, int warp, int lane,
+                                             int my_tiles, uint64_t* acc_full, volatile int* abort_flag,
+                                             const CUtensorMap* ugmap, const CUtensorMap* uvmap,
+                                             const CUtensorMap* dugmap, const CUtensorMap* duvmap, const GemmArgs& a,
+                                             RowOf row_of, ColOf col_base_of, Release release) {
+  using P = Pair<F16>;
+  constexpr int kSteps = 128 / kChunk;        // 16-column steps per warp per tile
+  const int ew = warp - kEpiWarp0;
+  const int quarter = ew % 4;
+  const int half = ew / 4;                    // which 128 of the tile's 256 F-columns
+  const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+  uint8_t* io = io_base + ew * kBwdIoBytes;   // [slot][u gate | u value], then du gate, du value
+  uint8_t* du_boxes = io + 2 * kUSlots * kBoxBytes;
+  uint64_t* ubar = &u_full[ew * kUSlots];
+  const int n_steps = my_tiles * kSteps;
+  auto slot = [&](uint8_t* box, int p) {
+    return reinterpret_cast<uint4*>(box + lane * 32 + ((p ^ ((lane >> 2) & 1)) << 4));
+  };
+  auto row0_of = [&](int i) { return row_of(i) + quarter * 32; };
+  auto col_of = [&](int i, int c) { return col_base_of(i) + half * 128 + c * kChunk; };
+  // step q's u boxes (gate and value columns of this warp's rows; zero past rows or F) into slot q % 3
+  auto load_u = [&](int q) {
+    if (lane == 0) {
+      const int i = q / kSteps, c = q % kSteps, r = q % kUSlots;
+      uint8_t* box = io + r * 2 * kBoxBytes;
+      mbar_arrive_expect_tx(&ubar[r], 2 * kBoxBytes);
+      tma_load_2d(box, ugmap, &ubar[r], col_of(i, c), row0_of(i));
+      tma_load_2d(box + kBoxBytes, uvmap, &ubar[r], col_of(i, c), row0_of(i));
+    }
+  };
+  int issued = 0;             // u loads issued (steps 0 .. issued - 1)
+  for (; issued < kUSlots - 1 && issued < n_steps; ++issued) load_u(issued);
+  bool ok = true;
+  int q = 0;                  // steps whose u has arrived
+  for (int i = 0; i < my_tiles && ok; ++i) {
+    const int acc = i & 1;
+    const int row0 = row0_of(i);
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&acc_full[acc], (i >> 1) & 1, abort_flag, a.spin_limit))) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    const uint32_t acc_addr = tmem + lane_addr + acc * kBwdBN + half * 128;
+#pragma unroll 1
+    for (int c = 0; c < kSteps; ++c) {
+      uint32_t gv[kChunk];
+      tmem_ld16(acc_addr + c * kChunk, gv);
+      tmem_wait_ld();
+      if (c + 1 == kSteps) {                  // the accumulator has been read: the MMA may reuse it
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) release(acc);
+      }
+      const int r = q % kUSlots;
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&ubar[r], (q / kUSlots) & 1, abort_flag, a.spin_limit))) {
+        ok = false;
+        break;
+      }
+      ++q;
+      uint8_t* ubox = io + r * 2 * kBoxBytes;
+      uint4 av[2], bv[2];
+#pragma unroll
+      for (int p2 = 0; p2 < 2; ++p2) {
+        av[p2] = *slot(ubox, p2);
+        bv[p2] = *slot(ubox + kBoxBytes, p2);
+      }
+      __syncwarp();                           // every lane has its u: slot r may be refilled
+      if (issued < n_steps) load_u(issued++); // two steps ahead, into the slot read one step ago
+      const uint32_t aw[8] = {av[0].x, av[0].y, av[0].z, av[0].w, av[1].x, av[1].y, av[1].z, av[1].w};
+      const uint32_t bw[8] = {bv[0].x, bv[0].y, bv[0].z, bv[0].w, bv[1].x, bv[1].y, bv[1].z, bv[1].w};
+      // per pair of columns: g rounded as the GEMM output, then gelu.cuh's geglu_grad arithmetic in
+      // its paired form
+      uint32_t dg[kChunk / 2], dv[kChunk / 2];
+#pragma unroll
+      for (int e = 0; e < kChunk / 2; ++e) {
+        const uint64_t g2 = widen<F16>(P::pack(__uint_as_float(gv[2 * e]), __uint_as_float(gv[2 * e + 1])));
+        const uint64_t a2 = widen<F16>(aw[e]);
+        const gelu::GeluParts2 pp = gelu::gelu_parts2(a2);
+        dv[e] = narrow<F16>(f2_mul(g2, widen<F16>(narrow<F16>(pp.gel))));                  // db
+        const uint64_t dgel = widen<F16>(narrow<F16>(f2_mul(g2, widen<F16>(bw[e]))));
+        dg[e] = narrow<F16>(gelu::geglu_dgate2(a2, pp.t, dgel));
+      }
+      if (lane == 0) bulk_wait_read_all();    // the previous step's du boxes have been read
+      __syncwarp();
+#pragma unroll
+      for (int p2 = 0; p2 < 2; ++p2) {
+        *slot(du_boxes, p2) = make_uint4(dg[4 * p2], dg[4 * p2 + 1], dg[4 * p2 + 2], dg[4 * p2 + 3]);
+        *slot(du_boxes + kBoxBytes, p2) = make_uint4(dv[4 * p2], dv[4 * p2 + 1], dv[4 * p2 + 2], dv[4 * p2 + 3]);
+      }
+      fence_async_shared();
+      __syncwarp();
+      const int col = col_of(i, c);
+      if (lane == 0 && col < a.F && row0 < a.rows) {
+        tma_store_2d(dugmap, du_boxes, col, row0);
+        tma_store_2d(duvmap, du_boxes + kBoxBytes, col, row0);
+        bulk_commit_group();
+      }
+    }
+  }
+  for (int j = q; j < issued; ++j)            // after an abort: the u loads in flight land first
+    for (uint32_t n = 0; n < a.spin_limit && !mbar_try_wait(&ubar[j % kUSlots], (j / kUSlots) & 1); ++n) {
+    }
+  if (lane == 0) bulk_wait_all();
+  return ok;
+}
+
 template <bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
 linear_geglu_bwd_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_constant__ CUtensorMap wmap,
@@ -625,104 +737,10 @@ linear_geglu_bwd_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_
     }
   } else if (warp >= kEpiWarp0) {
     // ------------------------------------------------------------ epilogue
-    using P = Pair<F16>;
-    constexpr int kSteps = 128 / kChunk;        // 16-column steps per warp per tile
-    const int ew = warp - kEpiWarp0;
-    const int quarter = ew % 4;
-    const int half = ew / 4;                    // which 128 of the tile's 256 F-columns
-    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    uint8_t* io = smem + kBwdIoOff + ew * kBwdIoBytes;   // [slot][u gate | u value], then du gate, du value
-    uint8_t* du_boxes = io + 2 * kUSlots * kBoxBytes;
-    uint64_t* ubar = &u_full[ew * kUSlots];
-    const int n_steps = my_tiles * kSteps;
-    auto slot = [&](uint8_t* box, int p) {
-      return reinterpret_cast<uint4*>(box + lane * 32 + ((p ^ ((lane >> 2) & 1)) << 4));
-    };
-    auto row0_of = [&](int i) { return (tile_of(i) / a.n_ftiles) * kBM + quarter * 32; };
-    auto col_of = [&](int i, int c) { return (tile_of(i) % a.n_ftiles) * kBwdBN + half * 128 + c * kChunk; };
-    // step q's u boxes (gate and value columns of this warp's rows; zero past rows or F) into slot q % 3
-    auto load_u = [&](int q) {
-      if (lane == 0) {
-        const int i = q / kSteps, c = q % kSteps, r = q % kUSlots;
-        uint8_t* box = io + r * 2 * kBoxBytes;
-        mbar_arrive_expect_tx(&ubar[r], 2 * kBoxBytes);
-        tma_load_2d(box, &ugmap, &ubar[r], col_of(i, c), row0_of(i));
-        tma_load_2d(box + kBoxBytes, &uvmap, &ubar[r], col_of(i, c), row0_of(i));
-      }
-    };
-    int issued = 0;             // u loads issued (steps 0 .. issued - 1)
-    for (; issued < kUSlots - 1 && issued < n_steps; ++issued) load_u(issued);
-    bool ok = true;
-    int q = 0;                  // steps whose u has arrived
-    for (int i = 0; i < my_tiles && ok; ++i) {
-      const int acc = i & 1;
-      const int row0 = row0_of(i);
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&acc_full[acc], (i >> 1) & 1, abort_flag, a.spin_limit))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t acc_addr = tmem + lane_addr + acc * kBwdBN + half * 128;
-#pragma unroll 1
-      for (int c = 0; c < kSteps; ++c) {
-        uint32_t gv[kChunk];
-        tmem_ld16(acc_addr + c * kChunk, gv);
-        tmem_wait_ld();
-        if (c + 1 == kSteps) {                  // the accumulator has been read: the MMA may reuse it
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[acc]);
-        }
-        const int r = q % kUSlots;
-        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&ubar[r], (q / kUSlots) & 1, abort_flag, a.spin_limit))) {
-          ok = false;
-          break;
-        }
-        ++q;
-        uint8_t* ubox = io + r * 2 * kBoxBytes;
-        uint4 av[2], bv[2];
-#pragma unroll
-        for (int p2 = 0; p2 < 2; ++p2) {
-          av[p2] = *slot(ubox, p2);
-          bv[p2] = *slot(ubox + kBoxBytes, p2);
-        }
-        __syncwarp();                           // every lane has its u: slot r may be refilled
-        if (issued < n_steps) load_u(issued++); // two steps ahead, into the slot read one step ago
-        const uint32_t aw[8] = {av[0].x, av[0].y, av[0].z, av[0].w, av[1].x, av[1].y, av[1].z, av[1].w};
-        const uint32_t bw[8] = {bv[0].x, bv[0].y, bv[0].z, bv[0].w, bv[1].x, bv[1].y, bv[1].z, bv[1].w};
-        // per pair of columns: g rounded as the GEMM output, then gelu.cuh's geglu_grad arithmetic in
-        // its paired form
-        uint32_t dg[kChunk / 2], dv[kChunk / 2];
-#pragma unroll
-        for (int e = 0; e < kChunk / 2; ++e) {
-          const uint64_t g2 = widen<F16>(P::pack(__uint_as_float(gv[2 * e]), __uint_as_float(gv[2 * e + 1])));
-          const uint64_t a2 = widen<F16>(aw[e]);
-          const gelu::GeluParts2 pp = gelu::gelu_parts2(a2);
-          dv[e] = narrow<F16>(f2_mul(g2, widen<F16>(narrow<F16>(pp.gel))));                  // db
-          const uint64_t dgel = widen<F16>(narrow<F16>(f2_mul(g2, widen<F16>(bw[e]))));
-          dg[e] = narrow<F16>(gelu::geglu_dgate2(a2, pp.t, dgel));
-        }
-        if (lane == 0) bulk_wait_read_all();    // the previous step's du boxes have been read
-        __syncwarp();
-#pragma unroll
-        for (int p2 = 0; p2 < 2; ++p2) {
-          *slot(du_boxes, p2) = make_uint4(dg[4 * p2], dg[4 * p2 + 1], dg[4 * p2 + 2], dg[4 * p2 + 3]);
-          *slot(du_boxes + kBoxBytes, p2) = make_uint4(dv[4 * p2], dv[4 * p2 + 1], dv[4 * p2 + 2], dv[4 * p2 + 3]);
-        }
-        fence_async_shared();
-        __syncwarp();
-        const int col = col_of(i, c);
-        if (lane == 0 && col < a.F && row0 < a.rows) {
-          tma_store_2d(&dugmap, du_boxes, col, row0);
-          tma_store_2d(&duvmap, du_boxes + kBoxBytes, col, row0);
-          bulk_commit_group();
-        }
-      }
-    }
-    for (int j = q; j < issued; ++j)            // after an abort: the u loads in flight land first
-      for (uint32_t n = 0; n < a.spin_limit && !mbar_try_wait(&ubar[j % kUSlots], (j / kUSlots) & 1); ++n) {
-      }
-    if (lane == 0) bulk_wait_all();
+    const bool ok = bwd_epilogue<F16>(
+        smem + kBwdIoOff, u_full, tmem, warp, lane, my_tiles, acc_full, abort_flag, &ugmap, &uvmap, &dugmap, &duvmap, a,
+        [&](int i) { return (tile_of(i) / a.n_ftiles) * kBM; }, [&](int i) { return (tile_of(i) % a.n_ftiles) * kBwdBN; },
+        [&](int acc) { mbar_arrive(&acc_empty[acc]); });
     if (!ok) watchdog_fire(kWdGemmEpilogue);
   }
 
@@ -730,6 +748,172 @@ linear_geglu_bwd_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+// ---------------------------------------------------------------- backward on CTA pairs (cta_group::2)
+// The backward on tiles of 256 rows x 256 F-columns shared by a cluster of two: each CTA loads its own
+// 128 rows of dy and half of the w columns (two 64-column boxes: the even CTA the first 128 columns of
+// the tile, the odd CTA the last 128), 32 KB per K block, five stages beside the epilogue's u/du boxes;
+// the even CTA issues M256 N256 K16 MMAs; each CTA's epilogue finishes its own 128 rows.
+constexpr int kPairBwdStages = 5;
+constexpr uint32_t kPairBwdStageBytes = kATile + 2 * kBwdWBox;
+constexpr uint32_t kPairBwdIoOff = kPairBwdStages * kPairBwdStageBytes;
+constexpr uint32_t kPairBwdBarOff = kPairBwdIoOff + kEpiWarps * kBwdIoBytes;
+constexpr int kPairBwdNumBars = 2 * kPairBwdStages + 2 + 2 + 1 + kEpiWarps * kUSlots;
+constexpr uint32_t kPairBwdMiscOff = kPairBwdBarOff + kPairBwdNumBars * 8;
+constexpr uint32_t kPairBwdSmem = kPairBwdMiscOff + 16 + 1024;
+static_assert(kPairBwdSmem <= 232448, "shared memory budget");
+
+template <bool F16>
+__global__ void __launch_bounds__(kThreads, 1)
+linear_geglu_bwd_pair_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_constant__ CUtensorMap wmap,
+                             const __grid_constant__ CUtensorMap ugmap, const __grid_constant__ CUtensorMap uvmap,
+                             const __grid_constant__ CUtensorMap dugmap, const __grid_constant__ CUtensorMap duvmap,
+                             const GemmArgs a) {
+  pdl_enter();   // before any global access and before claiming TMEM
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPairBwdBarOff);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kPairBwdStages;
+  uint64_t* acc_full = bars + 2 * kPairBwdStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint64_t* u_full = drain + 1;   // [epilogue warp][slot]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kPairBwdMiscOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kPairBwdMiscOff + 4);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const bool even = rank == 0;
+  const int pair = (int)blockIdx.x / 2, n_pairs = (int)gridDim.x / 2;
+  const int my_tiles = pair < a.n_tiles ? (a.n_tiles - 1 - pair) / n_pairs + 1 : 0;
+  auto tile_of = [&](int i) { return pair + i * n_pairs; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairBwdStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 2 * kEpiWarps);
+    }
+    mbar_init(drain, 1);
+    for (int w = 0; w < kEpiWarps * kUSlots; ++w) mbar_init(&u_full[w], 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&dymap);
+    prefetch_tensormap(&wmap);
+  }
+  if (warp == kEpiWarp0 && lane == 0) {
+    prefetch_tensormap(&ugmap);
+    prefetch_tensormap(&uvmap);
+    prefetch_tensormap(&dugmap);
+    prefetch_tensormap(&duvmap);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    bool ok = true;
+    int it = 0;
+    for (int i = 0; i < my_tiles && ok; ++i) {
+      const int t = tile_of(i);
+      const int m0 = (t / a.n_ftiles) * (2 * kBM) + (int)rank * kBM;
+      const int n0 = (t % a.n_ftiles) * kBwdBN + (int)rank * (kBwdBN / 2);   // this CTA's 128 columns
+      for (int kb = 0; kb < a.n_kb; ++kb, ++it) {
+        const int s = it % kPairBwdStages;
+        if (it >= kPairBwdStages && !__all_sync(0xffffffffu, mbar_wait_bounded(&empty[s], ((it / kPairBwdStages) - 1) & 1,
+                                                                                abort_flag, a.spin_limit))) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          uint8_t* st = smem + s * kPairBwdStageBytes;
+          const uint32_t bar = mapa_shared(&full[s], 0);
+          if (even) mbar_arrive_expect_tx(&full[s], 2 * kPairBwdStageBytes);
+          tma_load_2d_pair(st, &dymap, bar, kb * kBK, m0);
+          tma_load_2d_pair(st + kATile, &wmap, bar, n0, kb * kBK);
+          tma_load_2d_pair(st + kATile + kBwdWBox, &wmap, bar, n0 + 64, kb * kBK);
+        }
+        __syncwarp();
+      }
+    }
+    if (!ok) {
+      watchdog_fire(kWdGemmLoad);
+      if (even) drain_loads<kPairBwdStages>(full, it, a.spin_limit);
+    }
+  } else if (warp == 1 && even) {
+    // ------------------------------------------------------------ MMA issuer (even CTA, elected lane)
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, abort_flag, a.spin_limit));
+    };
+    constexpr uint32_t idesc = idesc_f16(2 * kBM, kBwdBN, F16 ? 0u : 1u, false, true);   // w MN-major
+    const uint64_t adesc0 = kmajor_sw128(smem_u32(smem));
+    const uint64_t bdesc0 = mnmajor_sw128(smem_u32(smem + kATile));
+    constexpr uint64_t kStageStep = kPairBwdStageBytes >> 4;
+    constexpr uint64_t kAKStep = 32 >> 4;
+    constexpr uint64_t kBKStep = (16 * 128) >> 4;
+    bool ok = true;
+    int it = 0;
+    for (int i = 0; i < my_tiles && ok; ++i) {
+      const int acc = i & 1;
+      if (i >= 2 && !wait(&acc_empty[acc], ((i >> 1) - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d = tmem + acc * kBwdBN;
+      for (int kb = 0; kb < a.n_kb; ++kb, ++it) {
+        const int s = it % kPairBwdStages;
+        if (!wait(&full[s], (it / kPairBwdStages) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t ad = adesc0 + (uint64_t)s * kStageStep;
+        const uint64_t bd = bdesc0 + (uint64_t)s * kStageStep;
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk)
+          mma_ss_pair_e(d, ad + kk * kAKStep, bd + kk * kBKStep, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+        mma_commit_pair_e(mapa_shared(&empty[s], 0));
+        mma_commit_pair_e(mapa_shared(&empty[s], 1));
+      }
+      if (!ok) break;
+      mma_commit_pair_e(mapa_shared(&acc_full[acc], 0));
+      mma_commit_pair_e(mapa_shared(&acc_full[acc], 1));
+    }
+    if (!ok && my_tiles > 0) watchdog_fire(kWdGemmMma);
+    mma_commit_pair_e(mapa_shared(drain, 0));
+    for (uint32_t i = 0; i < a.spin_limit && !mbar_try_wait(drain, 0); ++i) {
+    }
+  } else if (warp >= kEpiWarp0) {
+    // ------------------------------------------------------------ epilogue (both CTAs, own rows)
+    const bool ok = bwd_epilogue<F16>(
+        smem + kPairBwdIoOff, u_full, tmem, warp, lane, my_tiles, acc_full, abort_flag, &ugmap, &uvmap, &dugmap,
+        &duvmap, a, [&](int i) { return (tile_of(i) / a.n_ftiles) * (2 * kBM) + (int)rank * kBM; },
+        [&](int i) { return (tile_of(i) % a.n_ftiles) * kBwdBN; },
+        [&](int acc) {
+          if (even) mbar_arrive(&acc_empty[acc]);
+          else mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
+        });
+    if (!ok) watchdog_fire(kWdGemmEpilogue);
+  }
+
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem, kTmemCols);
 }
 
 // 2-D view (cols, rows) of a row-major 16-bit matrix with `pitch` elements between rows, copied in
@@ -828,6 +1012,60 @@ int launch(const CUtensorMap& xm, const CUtensorMap& wm, const CUtensorMap& ugm,
 }
 
 template <bool F16>
+int bwd_pair_clusters() {
+  static int cached[64];
+  static bool done[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (!done[dev]) {
+    auto kern = linear_geglu_bwd_pair_kernel<F16>;
+    int n = 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairBwdSmem) == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * 74);
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = kPairBwdSmem;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+    }
+    cudaGetLastError();
+    cached[dev] = n;
+    done[dev] = true;
+  }
+  return cached[dev];
+}
+
+template <bool F16>
+int launch_bwd_pair(const CUtensorMap& dym, const CUtensorMap& wm, const CUtensorMap& ugm, const CUtensorMap& uvm,
+                    const CUtensorMap& dugm, const CUtensorMap& duvm, const GemmArgs& a, int max_clusters,
+                    cudaStream_t stream) {
+  auto kern = linear_geglu_bwd_pair_kernel<F16>;
+  const int clusters = a.n_tiles < max_clusters ? a.n_tiles : max_clusters;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kPairBwdSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  KRSI_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, dym, wm, ugm, uvm, dugm, duvm, a));
+  return KRSI_OK;
+}
+
+template <bool F16>
 int launch_bwd(const CUtensorMap& dym, const CUtensorMap& wm, const CUtensorMap& ugm, const CUtensorMap& uvm,
                const CUtensorMap& dugm, const CUtensorMap& duvm, const GemmArgs& a, cudaStream_t stream) {
   auto kern = linear_geglu_bwd_kernel<F16>;
@@ -896,6 +1134,13 @@ extern "C" int krsi_linear_geglu_bwd(const void* dy, const void* w, const void* 
   if (n_rt * n_ft > INT32_MAX) return KRSI_ERR_UNSUPPORTED;
   GemmArgs a{nullptr, du, (int)rows, (int)K, (int)F, (int)n_ft, (int)(n_rt * n_ft), (int)((K + kBK - 1) / kBK),
              kSpinLimit};
+  const int clusters = rows > kBM ? (f16 ? bwd_pair_clusters<true>() : bwd_pair_clusters<false>()) : 0;
+  if (clusters > 0) {
+    GemmArgs pa = a;
+    pa.n_tiles = (int)(((rows + 2 * kBM - 1) / (2 * kBM)) * n_ft);
+    return f16 ? launch_bwd_pair<true>(dym, wm, ugm, uvm, dugm, duvm, pa, clusters, stream)
+               : launch_bwd_pair<false>(dym, wm, ugm, uvm, dugm, duvm, pa, clusters, stream);
+  }
   return f16 ? launch_bwd<true>(dym, wm, ugm, uvm, dugm, duvm, a, stream)
              : launch_bwd<false>(dym, wm, ugm, uvm, dugm, duvm, a, stream);
 }
