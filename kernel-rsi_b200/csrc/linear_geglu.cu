@@ -496,22 +496,24 @@ static_assert(kBwdSmem <= 232448, "shared memory budget");
 // next 64 columns one box further (LBO = 8 KB); the K step of 16 rows advances the start by 2 KB.
 __device__ __forceinline__ uint64_t mnmajor_sw128(uint32_t addr) { return smem_desc(addr, kBwdWBox, 1024, kSw128); }
 
-// The backward epilogue of one warp (warps kEpiWarp0.. of a CTA): for each of the CTA's tiles, read g
-// out of TMEM 16 columns at a time, hand the accumulator back (`release`), bring in the matching u
-// boxes through a ring of kUSlots (`io_base`: this CTA's per-warp boxes, `u_full`: their barriers),
-// and write du through staged boxes and TMA stores.  `row_of(i)` is the tile's first row handled by
-// this CTA, `col_base_of(i)` its first F-column.  Returns false after an abort.
-template <bool F16, typename RowOf, typename ColOf, typename Release>
+// The backward epilogue of one warp (warps kEpiWarp0.. of a CTA, NG groups of 4 warps): for each of
+// the CTA's tiles, read g out of TMEM 16 columns at a time (group g takes the 16-column chunks g,
+// g + NG, ...), hand the accumulator back (`release`), bring in the matching u boxes through a ring
+// of kUSlots (`io_base`: this CTA's per-warp boxes, `u_full`: their barriers), and write du through
+// staged boxes and TMA stores.  `row_of(i)` is the tile's first row handled by this CTA,
+// `col_base_of(i)` its first F-column.  Returns false after an abort.
+template <bool F16, int NG, typename RowOf, typename ColOf, typename Release>
 __device__ __forceinline__ bool bwd_epilogue(uint8_t* io_base, uint64_t* u_full, uint32_t tmem, int warp, int lane,
                                              int my_tiles, uint64_t* acc_full, volatile int* abort_flag,
                                              const CUtensorMap* ugmap, const CUtensorMap* uvmap,
                                              const CUtensorMap* dugmap, const CUtensorMap* duvmap, const GemmArgs& a,
                                              RowOf row_of, ColOf col_base_of, Release release) {
   using P = Pair<F16>;
-  constexpr int kSteps = 128 / kChunk;        // 16-column steps per warp per tile
+  constexpr int kChunks = kBwdBN / kChunk;    // 16-column chunks per tile
   const int ew = warp - kEpiWarp0;
   const int quarter = ew % 4;
-  const int half = ew / 4;                    // which 128 of the tile's 256 F-columns
+  const int grp = ew / 4;                     // chunks grp, grp + NG, ...
+  const int kSteps = (kChunks - grp + NG - 1) / NG;   // this warp's chunks per tile
   const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
   uint8_t* io = io_base + ew * kBwdIoBytes;   // [slot][u gate | u value], then du gate, du value
   uint8_t* du_boxes = io + 2 * kUSlots * kBoxBytes;
@@ -521,7 +523,7 @@ __device__ __forceinline__ bool bwd_epilogue(uint8_t* io_base, uint64_t* u_full,
     return reinterpret_cast<uint4*>(box + lane * 32 + ((p ^ ((lane >> 2) & 1)) << 4));
   };
   auto row0_of = [&](int i) { return row_of(i) + quarter * 32; };
-  auto col_of = [&](int i, int c) { return col_base_of(i) + half * 128 + c * kChunk; };
+  auto col_of = [&](int i, int c) { return col_base_of(i) + (grp + NG * c) * kChunk; };
   // step q's u boxes (gate and value columns of this warp's rows; zero past rows or F) into slot q % 3
   auto load_u = [&](int q) {
     if (lane == 0) {
@@ -544,11 +546,11 @@ __device__ __forceinline__ bool bwd_epilogue(uint8_t* io_base, uint64_t* u_full,
       break;
     }
     tc_fence_after();
-    const uint32_t acc_addr = tmem + lane_addr + acc * kBwdBN + half * 128;
+    const uint32_t acc_addr = tmem + lane_addr + acc * kBwdBN;
 #pragma unroll 1
     for (int c = 0; c < kSteps; ++c) {
       uint32_t gv[kChunk];
-      tmem_ld16(acc_addr + c * kChunk, gv);
+      tmem_ld16(acc_addr + (grp + NG * c) * kChunk, gv);
       tmem_wait_ld();
       if (c + 1 == kSteps) {                  // the accumulator has been read: the MMA may reuse it
         tc_fence_before();
@@ -737,7 +739,7 @@ linear_geglu_bwd_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_
     }
   } else if (warp >= kEpiWarp0) {
     // ------------------------------------------------------------ epilogue
-    const bool ok = bwd_epilogue<F16>(
+    const bool ok = bwd_epilogue<F16, kEpiWarps / 4>(
         smem + kBwdIoOff, u_full, tmem, warp, lane, my_tiles, acc_full, abort_flag, &ugmap, &uvmap, &dugmap, &duvmap, a,
         [&](int i) { return (tile_of(i) / a.n_ftiles) * kBM; }, [&](int i) { return (tile_of(i) % a.n_ftiles) * kBwdBN; },
         [&](int acc) { mbar_arrive(&acc_empty[acc]); });
@@ -755,17 +757,21 @@ linear_geglu_bwd_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_
 // 128 rows of dy and half of the w columns (two 64-column boxes: the even CTA the first 128 columns of
 // the tile, the odd CTA the last 128), 32 KB per K block, five stages beside the epilogue's u/du boxes;
 // the even CTA issues M256 N256 K16 MMAs; each CTA's epilogue finishes its own 128 rows.
-constexpr int kPairBwdStages = 5;
+// The epilogue (the GELU derivative on every element) bounds this kernel, so it runs 12 warps, three
+// per scheduler, where the operand stages' smaller footprint leaves room for their boxes.
+constexpr int kPairBwdStages = 4;
+constexpr int kPairBwdEpiWarps = 12;
+constexpr int kPairBwdThreads = (kEpiWarp0 + kPairBwdEpiWarps) * 32;   // 512: 128 registers per thread
 constexpr uint32_t kPairBwdStageBytes = kATile + 2 * kBwdWBox;
 constexpr uint32_t kPairBwdIoOff = kPairBwdStages * kPairBwdStageBytes;
-constexpr uint32_t kPairBwdBarOff = kPairBwdIoOff + kEpiWarps * kBwdIoBytes;
-constexpr int kPairBwdNumBars = 2 * kPairBwdStages + 2 + 2 + 1 + kEpiWarps * kUSlots;
+constexpr uint32_t kPairBwdBarOff = kPairBwdIoOff + kPairBwdEpiWarps * kBwdIoBytes;
+constexpr int kPairBwdNumBars = 2 * kPairBwdStages + 2 + 2 + 1 + kPairBwdEpiWarps * kUSlots;
 constexpr uint32_t kPairBwdMiscOff = kPairBwdBarOff + kPairBwdNumBars * 8;
 constexpr uint32_t kPairBwdSmem = kPairBwdMiscOff + 16 + 1024;
 static_assert(kPairBwdSmem <= 232448, "shared memory budget");
 
 template <bool F16>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kPairBwdThreads, 1)
 linear_geglu_bwd_pair_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_constant__ CUtensorMap wmap,
                              const __grid_constant__ CUtensorMap ugmap, const __grid_constant__ CUtensorMap uvmap,
                              const __grid_constant__ CUtensorMap dugmap, const __grid_constant__ CUtensorMap duvmap,
@@ -797,10 +803,10 @@ linear_geglu_bwd_pair_kernel(const __grid_constant__ CUtensorMap dymap, const __
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 2 * kEpiWarps);
+      mbar_init(&acc_empty[b], 2 * kPairBwdEpiWarps);
     }
     mbar_init(drain, 1);
-    for (int w = 0; w < kEpiWarps * kUSlots; ++w) mbar_init(&u_full[w], 1);
+    for (int w = 0; w < kPairBwdEpiWarps * kUSlots; ++w) mbar_init(&u_full[w], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -899,7 +905,7 @@ linear_geglu_bwd_pair_kernel(const __grid_constant__ CUtensorMap dymap, const __
     }
   } else if (warp >= kEpiWarp0) {
     // ------------------------------------------------------------ epilogue (both CTAs, own rows)
-    const bool ok = bwd_epilogue<F16>(
+    const bool ok = bwd_epilogue<F16, kPairBwdEpiWarps / 4>(
         smem + kPairBwdIoOff, u_full, tmem, warp, lane, my_tiles, acc_full, abort_flag, &ugmap, &uvmap, &dugmap,
         &duvmap, a, [&](int i) { return (tile_of(i) / a.n_ftiles) * (2 * kBM) + (int)rank * kBM; },
         [&](int i) { return (tile_of(i) % a.n_ftiles) * kBwdBN; },
@@ -1025,6 +1031,7 @@ int bwd_pair_clusters() {
       cfg.gridDim = dim3(2 * 74);
       cfg.blockDim = dim3(kThreads);
       cfg.dynamicSmemBytes = kPairBwdSmem;
+      cfg.blockDim = dim3(kPairBwdThreads);
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeClusterDimension;
       attr[0].val.clusterDim.x = 2;
@@ -1049,7 +1056,7 @@ int launch_bwd_pair(const CUtensorMap& dym, const CUtensorMap& wm, const CUtenso
   const int clusters = a.n_tiles < max_clusters ? a.n_tiles : max_clusters;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * clusters);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(kPairBwdThreads);
   cfg.dynamicSmemBytes = kPairBwdSmem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
