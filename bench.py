@@ -992,7 +992,13 @@ def main():
         from datetime import timedelta
 
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+        # NCCL's kernels run on a high-priority stream: the compute kernels are chained by dependent
+        # launches (the next grid is always pending), so at equal priority the block scheduler hands
+        # freed SMs to compute first and the gradient all-reduces wait for SMs
+        # (KRSI_NCCL_HIGH_PRIORITY=0 restores the default priority)
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.is_high_priority_stream = os.environ.get("KRSI_NCCL_HIGH_PRIORITY", "1") != "0"
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), pg_options=opts,
                                 device_id=torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0))))
     try:
         if args.impl == "reference":
