@@ -120,6 +120,7 @@ def main():
     ap.add_argument("--out", required=True)
     a = ap.parse_args()
     import geglu
+    import linear_geglu
     import relpos_attention as ra
     import rmsnorm
     import t5_bias
@@ -140,6 +141,9 @@ def main():
     pd = torch.randn(H, 2 * S - 1, device=dev)
     cases["relpos_attention"] = (lambda q, p: ra.relpos_attention(q, p, B, S, H, D, 1.0),
                                  lambda q, p: ra.reference(q, p, B, S, H, D, 1.0), [qkv, pd])
+    xl = torch.randn(2048, 768, device=dev, dtype=torch.bfloat16)
+    wl = (torch.randn(2 * 2048, 768, device=dev) * 768 ** -0.5).to(torch.bfloat16)
+    cases["linear_geglu"] = (linear_geglu.linear_geglu, linear_geglu.reference, [xl, wl])
     table = 0.1 * torch.randn(32, 12, device=dev)
     cases["t5_bias"] = (lambda t: t5_bias.t5_relpos_bias(t, 512), lambda t: t5_bias.reference(t, 512), [table])
     out = {"versions": info, "library": {}, "regions": {},
