@@ -902,7 +902,8 @@ def run_krsi_arm(args, rank, world):
     finally:
         release(wl)
     if args.workload == "block" and world == 1 and not args.no_ops:
-        # configs 1-4 on the same GPU, each graph-timed with its roofline and CPU baseline
+        # configs 1-4 and the fused projection on the same GPU, each graph-timed with its roofline
+        # and CPU baseline
         ops = {}
         for name in OPS_IN_DEFAULT_LINE:
             owl = WORKLOADS[name](rank, world)
@@ -976,7 +977,7 @@ def main():
     ap.add_argument("--impl", default="krsi", choices=["krsi", "reference"])
     ap.add_argument("--workload", default=os.environ.get("KRSI_BENCH_WORKLOAD", "block"), choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-ops", action="store_true", help="block at N=1: skip the configs 1-4 `ops` object")
+    ap.add_argument("--no-ops", action="store_true", help="block at N=1: skip the `ops` object (configs 1-4, linear_geglu)")
     ap.add_argument("--profile-case", nargs="+", metavar="ARG",
                     help="KIND N [S]: rmsnorm|rmsnorm_bf16 ROWS, geglu ROWS, attn|attn_fwd B S, t5_bias S")
     args = ap.parse_args()

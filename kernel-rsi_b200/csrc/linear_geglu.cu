@@ -23,6 +23,10 @@
 // Measured on B200 at [32768 x 1152] x [9216 x 1152]: the mainloop alone runs at 1521 TFLOP/s;
 // storing u straight from registers (one row per lane: 32 lines per warp store) held the epilogue
 // back to 894 TFLOP/s for the whole op, which the staged TMA stores remove.
+// This one-CTA kernel serves up to 128 rows; larger problems run linear_geglu_pair_kernel (below):
+// the same roles on tiles of 256 rows shared by the two CTAs of a cluster (cta_group::2), each CTA
+// loading half of the operands.  The file also holds the backward, GEGLU's backward in the epilogue
+// of the down projection's input gradient (linear_geglu_bwd_kernel, linear_geglu_bwd_pair_kernel).
 // Every wait is bounded (watchdog.cuh); a stalled pipeline ends the CTA with an error word.
 #include <string.h>
 
