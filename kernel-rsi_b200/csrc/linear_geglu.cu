@@ -30,6 +30,8 @@
 // Every wait is bounded (watchdog.cuh); a stalled pipeline ends the CTA with an error word.
 #include <string.h>
 
+#include <atomic>
+
 #include "attn_common.cuh"
 #include "common.cuh"
 #include "gelu.cuh"
@@ -960,16 +962,16 @@ bool box_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64
 // device, queried once.
 template <bool F16>
 int pair_clusters() {
-  static int cached[64];
-  static bool done[64];
+  static std::atomic<int> cached[64];   // clusters + 1 once queried (0: not yet); races only repeat the query
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
-  if (!done[dev]) {
+  int v = cached[dev].load(std::memory_order_relaxed);
+  if (v == 0) {
     auto kern = linear_geglu_pair_kernel<F16>;
     int n = 0;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmem) == cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(2 * 74);
+      cfg.gridDim = dim3(2 * (device_sm_count() / 2));
       cfg.blockDim = dim3(kThreads);
       cfg.dynamicSmemBytes = kPairSmem;
       cudaLaunchAttribute attr[1];
@@ -982,10 +984,10 @@ int pair_clusters() {
       if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
     }
     cudaGetLastError();   // a refused query leaves no sticky error behind
-    cached[dev] = n;
-    done[dev] = true;
+    v = n + 1;
+    cached[dev].store(v, std::memory_order_relaxed);
   }
-  return cached[dev];
+  return v - 1;
 }
 
 template <bool F16>
@@ -1023,16 +1025,16 @@ int launch(const CUtensorMap& xm, const CUtensorMap& wm, const CUtensorMap& ugm,
 
 template <bool F16>
 int bwd_pair_clusters() {
-  static int cached[64];
-  static bool done[64];
+  static std::atomic<int> cached[64];   // clusters + 1 once queried (0: not yet); races only repeat the query
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
-  if (!done[dev]) {
+  int v = cached[dev].load(std::memory_order_relaxed);
+  if (v == 0) {
     auto kern = linear_geglu_bwd_pair_kernel<F16>;
     int n = 0;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairBwdSmem) == cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(2 * 74);
+      cfg.gridDim = dim3(2 * (device_sm_count() / 2));
       cfg.blockDim = dim3(kThreads);
       cfg.dynamicSmemBytes = kPairBwdSmem;
       cfg.blockDim = dim3(kPairBwdThreads);
@@ -1046,10 +1048,10 @@ int bwd_pair_clusters() {
       if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
     }
     cudaGetLastError();
-    cached[dev] = n;
-    done[dev] = true;
+    v = n + 1;
+    cached[dev].store(v, std::memory_order_relaxed);
   }
-  return cached[dev];
+  return v - 1;
 }
 
 template <bool F16>
