@@ -358,7 +358,7 @@ class LinearGegluWorkload(OpWorkload):
     ROWS, K, F = 32768, 1152, 4608
     work_per_call = 2 * ROWS * K * 2 * F
     launches_per_call = 1
-    kernel_key = "linear_geglu_kernel"
+    kernel_key = "linear_geglu_pair_kernel"
     in_bytes = (ROWS * K + 2 * F * K) * 2
 
     def config(self):
