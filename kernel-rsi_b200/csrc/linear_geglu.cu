@@ -28,6 +28,7 @@
 // loading half of the operands.  The file also holds the backward, GEGLU's backward in the epilogue
 // of the down projection's input gradient (linear_geglu_bwd_kernel, linear_geglu_bwd_pair_kernel).
 // Every wait is bounded (watchdog.cuh); a stalled pipeline ends the CTA with an error word.
+#include <stdlib.h>
 #include <string.h>
 
 #include <atomic>
@@ -960,6 +961,14 @@ bool box_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64
 
 // Clusters of two of the pair kernel that fit on the device at once (0: no pair launch possible), per
 // device, queried once.
+// KRSI_GEMM_PAIRS=0 in the environment runs the one-CTA kernels for every size (for a device partition
+// that cannot schedule clusters of two, or to compare the two paths, which give the same bits).  Read
+// on every call.
+inline bool pairs_enabled() {
+  const char* v = getenv("KRSI_GEMM_PAIRS");
+  return v == nullptr || strcmp(v, "0") != 0;
+}
+
 template <bool F16>
 int pair_clusters() {
   static std::atomic<int> cached[64];   // clusters + 1 once queried (0: not yet); races only repeat the query
@@ -1115,7 +1124,7 @@ extern "C" int krsi_linear_geglu_fwd(const void* x, const void* w, void* u, void
   GemmArgs a{u, out, (int)rows, (int)K, (int)F, (int)n_ft, (int)(n_rt * n_ft), (int)((K + kBK - 1) / kBK),
              kSpinLimit};
   // More than one row tile: CTA pairs (M = 256 tiles), when the device runs clusters of two of them.
-  const int clusters = rows > kBM ? (f16 ? pair_clusters<true>() : pair_clusters<false>()) : 0;
+  const int clusters = rows > kBM && pairs_enabled() ? (f16 ? pair_clusters<true>() : pair_clusters<false>()) : 0;
   if (clusters > 0) {
     GemmArgs pa = a;
     pa.n_tiles = (int)(((rows + 2 * kBM - 1) / (2 * kBM)) * n_ft);
@@ -1147,7 +1156,8 @@ extern "C" int krsi_linear_geglu_bwd(const void* dy, const void* w, const void* 
   if (n_rt * n_ft > INT32_MAX) return KRSI_ERR_UNSUPPORTED;
   GemmArgs a{nullptr, du, (int)rows, (int)K, (int)F, (int)n_ft, (int)(n_rt * n_ft), (int)((K + kBK - 1) / kBK),
              kSpinLimit};
-  const int clusters = rows > kBM ? (f16 ? bwd_pair_clusters<true>() : bwd_pair_clusters<false>()) : 0;
+  const int clusters =
+      rows > kBM && pairs_enabled() ? (f16 ? bwd_pair_clusters<true>() : bwd_pair_clusters<false>()) : 0;
   if (clusters > 0) {
     GemmArgs pa = a;
     pa.n_tiles = (int)(((rows + 2 * kBM - 1) / (2 * kBM)) * n_ft);

@@ -29,6 +29,7 @@ def inputs(rows, K, F, dt, seed):
 @pytest.mark.parametrize("rows,K,F,dt", [
     (2048, 1152, 4608, torch.bfloat16),   # the block's feed-forward: d 1152 -> 2 x 4608
     (300, 1152, 4608, torch.bfloat16),    # ragged last row tile
+    (128, 1152, 4608, torch.bfloat16),    # the largest size on the one-CTA kernel
     (1, 64, 8, torch.bfloat16),           # one row, one partial F tile
     (129, 72, 200, torch.bfloat16),       # K not a multiple of 64, F not a multiple of 128
     (257, 1000, 136, torch.bfloat16),
@@ -125,6 +126,7 @@ def test_c_abi_direct_call_and_errors():
 @pytest.mark.parametrize("rows,K,F,dt", [
     (2048, 1152, 4608, torch.bfloat16),   # the block's down projection: dy [rows, 1152], wo [1152, 4608]
     (300, 1152, 4608, torch.bfloat16),    # ragged last row tile
+    (128, 1152, 4608, torch.bfloat16),    # the largest size on the one-CTA kernel
     (1, 64, 8, torch.bfloat16),
     (129, 72, 200, torch.bfloat16),       # K not a multiple of 64, F not a multiple of 256
     (257, 1000, 136, torch.bfloat16),
@@ -204,3 +206,24 @@ def test_bwd_c_abi_and_errors():
     assert lib.krsi_linear_geglu_bwd(ptr(dy), ptr(w), ptr(u), ptr(du), ctypes.c_int64(64), ctypes.c_int64(250),
                                      ctypes.c_int64(128), DT[torch.bfloat16], stream()) == 2
     assert lib.krsi_linear_geglu_bwd(ptr(dy), ctypes.c_void_p(w.data_ptr() + 8), ptr(u), ptr(du), *args) == 3
+
+
+@pytest.mark.parametrize("rows,K,F", [(129, 72, 200), (256, 1152, 4608), (300, 1152, 4608), (2048, 768, 2048)])
+def test_cta_pairs_match_one_cta_kernels_bitwise(rows, K, F, monkeypatch):
+    """Above 128 rows the fused kernels run on CTA pairs (M = 256 tiles split over two CTAs); each CTA
+    runs the same K loop as the one-CTA kernel, so both paths give the same bits (KRSI_GEMM_PAIRS=0
+    forces the one-CTA kernels)."""
+    x, w, _ = inputs(rows, K, F, torch.bfloat16, seed=rows + 7)
+    x, w = x.to(dev), w.to(dev)
+    dy = O.gen((rows, K), rows + 8).to(dev, torch.bfloat16)
+    wo = O.gen((K, F), rows + 9, std=K ** -0.5).to(dev, torch.bfloat16)
+    monkeypatch.setenv("KRSI_GEMM_PAIRS", "1")
+    u_p, o_p = torch.ops.krsi.linear_geglu_fwd(x, w)
+    du_p = torch.ops.krsi.linear_geglu_bwd(dy, wo, u_p)
+    monkeypatch.setenv("KRSI_GEMM_PAIRS", "0")
+    u_1, o_1 = torch.ops.krsi.linear_geglu_fwd(x, w)
+    du_1 = torch.ops.krsi.linear_geglu_bwd(dy, wo, u_p)
+    assert torch.equal(u_p, u_1) and torch.equal(o_p, o_1)
+    assert torch.equal(du_p, du_1)
+    import _ext
+    assert _ext.device_status() == 0
