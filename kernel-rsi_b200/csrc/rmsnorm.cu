@@ -131,7 +131,9 @@ __device__ __forceinline__ int acc_idx(int c, int e, int t) { return ((c * (VEC 
 // cp.async while the current row is reduced and stored, so a warp always has a row in flight
 // (the loads of the plain loop wait a full DRAM round trip per row).  Each lane copies and
 // later reads only its own 16-byte packets, so cp.async.wait_group is the only
-// synchronisation.  Stage: per warp, [x | g][NCH][32 lanes] of 16 bytes.
+// synchronisation.  Stage: per warp, [x | g][NCH][32 lanes] of 16 bytes, and a third part for the
+// added gradient when there is one (read at the dx store, refilled after it: measured at the block
+// shape, loading it from global memory at the store cost a DRAM round trip per row).
 template <int XT, int TPR, int VEC, int NCH>
 constexpr bool kBwdStage = kBwdSmemAcc<TPR, VEC, NCH> && sizeof(typename Elem<XT>::T) == 2 && VEC == 8;
 
@@ -162,8 +164,9 @@ rms_bwd_kernel(const typename Elem<XT>::T* __restrict__ g, const typename Elem<X
 
   constexpr bool SACC = kBwdSmemAcc<TPR, VEC, NCH>;
   constexpr bool STAGE = kBwdStage<XT, TPR, VEC, NCH>;
-  // STAGE: this warp's stage, after the RPB accumulators
-  uint4* stg = reinterpret_cast<uint4*>(smem_dw + RPB * (NCH * VEC * 32)) + sub * (2 * NCH * 32);
+  // STAGE: this warp's stage, after the RPB accumulators; [x | g | gadd] when gadd is staged
+  const bool sga = STAGE && gadd != nullptr;
+  uint4* stg = reinterpret_cast<uint4*>(smem_dw + RPB * (NCH * VEC * 32)) + sub * ((sga ? 3 : 2) * NCH * 32);
   float dwv[NCH][VEC];
 #pragma unroll
   for (int c = 0; c < NCH; ++c)
@@ -186,6 +189,7 @@ rms_bwd_kernel(const typename Elem<XT>::T* __restrict__ g, const typename Elem<X
       if (row < rows && col < n) {
         cp_async16(&stg[c * 32 + t], x + row * n + col);
         cp_async16(&stg[(NCH + c) * 32 + t], g + row * n + col);
+        if (sga) cp_async16(&stg[(2 * NCH + c) * 32 + t], gadd + row * n + col);
       }
     }
     cp_async_commit();
@@ -273,13 +277,30 @@ rms_bwd_kernel(const typename Elem<XT>::T* __restrict__ g, const typename Elem<X
           for (int e = 0; e < VEC; ++e) o[e] = r * dn[c][e] - xv[c][e] * k;
           if (gadd != nullptr) {   // a second gradient of x (a residual branch), added before rounding
             float ga[VEC];
-            load_vec<XT, VEC>(gadd + row * n + col, ga, true);
+            if (sga) {
+              using E = Elem<XT>;
+              Vec16<typename E::T> vga;
+              *reinterpret_cast<uint4*>(&vga) = stg[(2 * NCH + c) * 32 + t];
+#pragma unroll
+              for (int e = 0; e < VEC; ++e) ga[e] = E::load(vga.v[e]);
+            } else {
+              load_vec<XT, VEC>(gadd + row * n + col, ga, true);
+            }
 #pragma unroll
             for (int e = 0; e < VEC; ++e) o[e] += ga[e];
           }
           store_vec<XT, VEC>(dxr + col, o);
         }
       }
+    }
+    if (sga) {   // the added gradient's slots were read above: refill them with the next row's
+      __syncwarp();
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        const int col = (c * TPR + t) * VEC;
+        if (nrow < rows && col < n) cp_async16(&stg[(2 * NCH + c) * 32 + t], gadd + nrow * n + col);
+      }
+      cp_async_commit();
     }
   }
 
@@ -423,7 +444,8 @@ template <int XT, int WT, int TPR, int VEC, int NCH>
 int run_bwd(const BwdArgs& a) {
   using Cfg = RowCfg<TPR>;
   const size_t per_warp = kBwdSmemAcc<TPR, VEC, NCH> ? (size_t)NCH * VEC * 32 : (size_t)a.n;
-  const size_t stage = kBwdStage<XT, TPR, VEC, NCH> ? (size_t)Cfg::kRowsPerBlock * 2 * NCH * 32 * 16 : 0;
+  const size_t stage =
+      kBwdStage<XT, TPR, VEC, NCH> ? (size_t)Cfg::kRowsPerBlock * (a.gadd ? 3 : 2) * NCH * 32 * 16 : 0;
   const size_t smem =
       Cfg::kRowsPerBlock > 1 ? (size_t)Cfg::kRowsPerBlock * per_warp * sizeof(float) + stage : 0;
   auto kern = rms_bwd_kernel<XT, WT, TPR, VEC, NCH>;
