@@ -90,7 +90,19 @@ struct FwdArgs {
   int n_qp;           // query pairs (work items per head)
   uint32_t spin_limit;
   int out32_v8;       // out32 is 32-byte aligned: 256-bit stores
+  uint32_t obox_off;  // shared-memory offset of the output staging boxes (0: per-thread stores)
 };
+
+// Output staging: each softmax warp writes its 32 rows of O in 16-column chunks into two boxes, the
+// fp32 one [32 rows x 16] (64-byte rows, 64-byte swizzle) and the 16-bit one [32 x 16] (32-byte rows,
+// 32-byte swizzle), and one lane stores both with TMA (maps over (D, H, S, B): columns past D and rows
+// past S are clipped).  Measured against per-thread stores (32 rows per warp instruction), same box:
+// 29.8 vs 31.0 us at B 2 S 1024, 299.7 vs 304.2 us at B 8 S 2048, 343.1 vs 341.5 us at B 32 S 1024.
+// (With the output stores removed altogether the last took 283.5 us: most of their cost is the
+// 226 MB of HBM writes themselves, which staging cannot remove.)
+constexpr uint32_t kOBox32 = 32 * 16 * 4;
+constexpr uint32_t kOBoxWarp = kOBox32 + 32 * 16 * 2;   // 3 KB per softmax warp
+constexpr uint32_t kOBoxBytes = 8 * kOBoxWarp;
 
 // Bias windows.  The bias of (query q, key k) is pd[h, k - q + S - 1].  A work item (queries q0 ..
 // q0 + 255, all keys) forms indices kRowPad + k - q + S - 1 in [w0 + 2, w0 + win_floats - 4] with
@@ -124,7 +136,8 @@ __device__ __forceinline__ void fill_shifted(float* dst, int n, int off, const f
 // in the background by warps 2-3.
 template <int DP, bool F16, bool RES>
 __global__ void __launch_bounds__(kThreads, 1)
-relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
+relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap o32map,
+                  const __grid_constant__ CUtensorMap o16map, const FwdArgs a) {
   pdl_enter();   // before any global access and before claiming TMEM
   using C = FwdCfg<DP>;
   constexpr int NS = C::NS;
@@ -551,6 +564,41 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
           tc_fence_before();
           mbar_arrive(&o_free[t]);
         }
+        if (a.obox_off != 0) {   // staged: boxes of 16 columns, two TMA stores per chunk
+          uint8_t* box32 = smem + a.obox_off + (warp - 4) * kOBoxWarp;
+          uint8_t* box16 = box32 + kOBox32;
+          const int qrow0 = q0 + t * kTileRows + quarter * 32;   // the warp's first row
+#pragma unroll
+          for (int c = 0; c < kGrp; c += 16) {
+            if (c0 + c >= a.D) break;   // warp-uniform
+            if (lane == 0) bulk_wait_read_all();   // the previous chunk's boxes have been read
+            __syncwarp();
+            const float* f = ofin + c;
+            uint4* b32 = reinterpret_cast<uint4*>(box32 + lane * 64);
+#pragma unroll
+            for (int p4 = 0; p4 < 4; ++p4)
+              b32[p4 ^ ((lane >> 1) & 3)] = make_uint4(__float_as_uint(f[4 * p4]), __float_as_uint(f[4 * p4 + 1]),
+                                                       __float_as_uint(f[4 * p4 + 2]), __float_as_uint(f[4 * p4 + 3]));
+            uint4* b16 = reinterpret_cast<uint4*>(box16 + lane * 32);
+#pragma unroll
+            for (int p8 = 0; p8 < 2; ++p8) {
+              const float* h8 = f + 8 * p8;
+              b16[p8 ^ ((lane >> 2) & 1)] =
+                  F16 ? make_uint4(pack_f16x2(h8[0], h8[1]), pack_f16x2(h8[2], h8[3]), pack_f16x2(h8[4], h8[5]),
+                                   pack_f16x2(h8[6], h8[7]))
+                      : make_uint4(pack_bf16x2(h8[0], h8[1]), pack_bf16x2(h8[2], h8[3]),
+                                   pack_bf16x2(h8[4], h8[5]), pack_bf16x2(h8[6], h8[7]));
+            }
+            fence_async_shared();   // staged boxes -> visible to the TMA unit
+            __syncwarp();
+            if (lane == 0 && qrow0 < a.S) {
+              tma_store_4d(&o32map, box32, c0 + c, bh % a.H, qrow0, b);
+              tma_store_4d(&o16map, box16, c0 + c, bh % a.H, qrow0, b);
+              bulk_commit_group();
+            }
+          }
+          continue;
+        }
 #pragma unroll
         for (int c = 0; c < kGrp; c += 8) {
           if (row_ok && c0 + c < a.D) {   // D is a multiple of 8: whole 8-column groups are in or out
@@ -575,6 +623,7 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
       }
       if (row_ok) a.lse[(size_t)bh * a.S + q] = m_run + __log2f(l_run);
     }
+    if (a.obox_off != 0 && lane == 0) bulk_wait_all();   // every output store has completed
     if (!ok) watchdog_fire(kWdFwdSoftmax);
   }
 
@@ -586,28 +635,54 @@ relpos_fwd_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs a) {
 
 constexpr size_t kMaxSmem = 232448;   // 227 KB per CTA on sm_100
 
+// 4-D view (D, H, S, B) of a [B*S, H*D] output (element size es) for the staging boxes' TMA stores:
+// box (16, 1, 32, 1), so a store clips at column D of its head and at row S of its sequence.
+bool make_out_box_map(CUtensorMap* map, const void* base, int64_t B, int64_t S, int64_t H, int64_t D, int es,
+                      CUtensorMapDataType dt, CUtensorMapSwizzle sw) {
+  attn::EncodeTiledFn enc = attn::encode_fn();
+  if (!enc) return false;
+  memset(map, 0, sizeof(*map));
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)(D * es), (cuuint64_t)(H * D * es), (cuuint64_t)(S * H * D * es)};
+  cuuint32_t box[4] = {16, 1, 32, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return enc(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int DP, bool F16>
-int launch_fwd(const CUtensorMap& tmap, const FwdArgs& a, cudaStream_t stream) {
+int launch_fwd(const CUtensorMap& tmap, const CUtensorMap& o32map, const CUtensorMap& o16map, FwdArgs a,
+               bool maps_ok, cudaStream_t stream) {
   using C = FwdCfg<DP>;
   const size_t res_smem = C::kSmem + (size_t)win_bytes(a.S);
   const bool res = res_smem <= kMaxSmem;
   auto kern = res ? relpos_fwd_kernel<DP, F16, true> : relpos_fwd_kernel<DP, F16, false>;
-  const size_t smem = res ? res_smem : C::kSmem;
+  size_t smem = res ? res_smem : C::kSmem;
+  // the output staging boxes after everything else (512-byte aligned for the 64-byte swizzle), when
+  // they fit; smem - 1024 is the layout's end (the last 1024 bytes are alignment slack)
+  const size_t box_off = (smem - 1024 + 511) & ~size_t(511);
+  if (maps_ok && box_off + kOBoxBytes + 1024 <= kMaxSmem) {
+    a.obox_off = (uint32_t)box_off;
+    smem = box_off + kOBoxBytes + 1024;
+  } else {
+    a.obox_off = 0;
+  }
   KRSI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int64_t items = (int64_t)a.B * a.H * a.n_qp;   // persistent: at most one CTA per SM
   const int grid = (int)(items < device_sm_count() ? items : device_sm_count());
-  KRSI_CUDA_TRY(launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, tmap, a));
+  KRSI_CUDA_TRY(launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, tmap, o32map, o16map, a));
   return KRSI_OK;
 }
 
 template <bool F16>
-int dispatch_dp(int DP, const CUtensorMap& tmap, const FwdArgs& a, cudaStream_t s) {
+int dispatch_dp(int DP, const CUtensorMap& tmap, const CUtensorMap& o32m, const CUtensorMap& o16m, const FwdArgs& a,
+                bool maps_ok, cudaStream_t s) {
   switch (DP) {
-    case 32: return launch_fwd<32, F16>(tmap, a, s);
-    case 64: return launch_fwd<64, F16>(tmap, a, s);
-    case 80: return launch_fwd<80, F16>(tmap, a, s);
-    case 96: return launch_fwd<96, F16>(tmap, a, s);
-    case 128: return launch_fwd<128, F16>(tmap, a, s);
+    case 32: return launch_fwd<32, F16>(tmap, o32m, o16m, a, maps_ok, s);
+    case 64: return launch_fwd<64, F16>(tmap, o32m, o16m, a, maps_ok, s);
+    case 80: return launch_fwd<80, F16>(tmap, o32m, o16m, a, maps_ok, s);
+    case 96: return launch_fwd<96, F16>(tmap, o32m, o16m, a, maps_ok, s);
+    case 128: return launch_fwd<128, F16>(tmap, o32m, o16m, a, maps_ok, s);
     default: return KRSI_ERR_UNSUPPORTED;
   }
 }
@@ -647,6 +722,15 @@ extern "C" int krsi_relpos_attn_fwd(const void* qkv, int64_t qkv_row_stride, con
   if (B * H * ((S + kItemRows - 1) / kItemRows) > INT32_MAX) return KRSI_ERR_UNSUPPORTED;
   FwdArgs a{pd, out, out32, lse, (int)B, (int)S, (int)H, (int)D, scale * 1.4426950408889634f,
             (int)((S + kBN - 1) / kBN), (int)((S + kItemRows - 1) / kItemRows), kSpinLimit,
-            (reinterpret_cast<uintptr_t>(out32) & 31) == 0 ? 1 : 0};
-  return dtype == KRSI_F16 ? dispatch_dp<true>(DP, tmap, a, stream) : dispatch_dp<false>(DP, tmap, a, stream);
+            (reinterpret_cast<uintptr_t>(out32) & 31) == 0 ? 1 : 0, 0u};
+  CUtensorMap o32m, o16m;
+  const bool maps_ok = make_out_box_map(&o32m, out32, B, S, H, D, 4, CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                                        CU_TENSOR_MAP_SWIZZLE_64B) &&
+                       make_out_box_map(&o16m, out, B, S, H, D, 2,
+                                        dtype == KRSI_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                          : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                                        CU_TENSOR_MAP_SWIZZLE_32B);
+  if (!maps_ok) memset(&o32m, 0, sizeof(o32m)), memset(&o16m, 0, sizeof(o16m));
+  return dtype == KRSI_F16 ? dispatch_dp<true>(DP, tmap, o32m, o16m, a, maps_ok, stream)
+                           : dispatch_dp<false>(DP, tmap, o32m, o16m, a, maps_ok, stream);
 }
