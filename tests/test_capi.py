@@ -58,6 +58,25 @@ def test_argument_checks_return_codes(lib):
     assert lib.krsi_geglu_fwd(vp(0), vp(0), i64(0), i64(8), 1, vp(0)) == 0
 
 
+def test_empty_inputs_launch_nothing(lib):
+    """Zero rows, batch or sequence length return success before any pointer check or CUDA call
+    (the cases with an output to zero, an RMSNorm dw or a T5 table gradient, need a device)."""
+    i64, vp, f32 = ctypes.c_int64, ctypes.c_void_p, ctypes.c_float
+    assert lib.krsi_geglu_bwd(vp(0), vp(0), vp(0), i64(0), i64(8), 1, vp(0)) == 0
+    assert lib.krsi_geglu_bwd(vp(0), vp(0), vp(0), i64(4), i64(0), 1, vp(0)) == 0
+    for B, S in ((0, 128), (2, 0), (0, 0)):
+        assert lib.krsi_relpos_attn_fwd(vp(0), i64(3 * 16 * 72), vp(0), vp(0), vp(0), vp(0), i64(B), i64(S),
+                                        i64(16), i64(72), f32(72 ** -0.5), 1, vp(0)) == 0, (B, S)
+    assert lib.krsi_relpos_attn_bwd(vp(0), vp(0), i64(3 * 16 * 72), vp(0), vp(0), vp(0), vp(0), i64(3 * 16 * 72),
+                                    vp(0), vp(0), ctypes.c_size_t(0), i64(2), i64(0), i64(16), i64(72),
+                                    f32(72 ** -0.5), 1, vp(0)) == 0
+    assert lib.krsi_t5_bias_fwd(vp(0), vp(0), i64(0), i64(12), 32, 128, 1, 0, vp(0)) == 0
+    # a negative size is an argument error, not an empty input
+    assert lib.krsi_relpos_attn_fwd(vp(0), i64(3 * 16 * 72), vp(0), vp(0), vp(0), vp(0), i64(-1), i64(128),
+                                    i64(16), i64(72), f32(72 ** -0.5), 1, vp(0)) == 1
+    assert lib.krsi_geglu_bwd(vp(0), vp(0), vp(0), i64(-1), i64(8), 1, vp(0)) == 1
+
+
 def test_workspace_queries(lib):
     sz = ctypes.c_size_t(0)
     assert lib.krsi_rmsnorm_bwd_workspace_size(ctypes.c_int64(2048), ctypes.c_int64(1152), ctypes.byref(sz)) == 0
